@@ -1,0 +1,383 @@
+"""Benchmark of the paged-attention decode hot path on B200.
+
+One step = reshape_and_cache of each sequence's new token + paged-attention decode over the
+whole batch (256 sequences, lognormal contexts median 1024 clipped to [16, 4096], GQA 32/8,
+head_dim 128, block size 16, bf16, shuffled block pool), one layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own independent config-2 batch (the
+path partitions by sequence; no data-path collective), so scaling is weak and `value` is the sum
+of all ranks' bytes over the max-over-ranks time.  The reference arm (`--impl reference`) times
+the reference's own CPU kernel (oracle/_ref, compiled from the reference's sources; the oracle's
+C restatement when that build is absent) on the host cores, rank 0 only.
+
+Metric: algorithmic HBM GB/s of the step (bytes every step must move: each context token's K and
+V once per KV head, queries, outputs, block tables, lengths, the new K/V rows and slots).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged-attn decode HBM GB/s (% of peak); engine tokens/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per decode launch from the committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", "paged_decode_config2.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def step_bytes(b, elem=2):
+    """Algorithmic bytes of one step (decode + the new-token cache write)."""
+    ctx = b.context_lens.astype(np.int64)
+    kv = int(ctx.sum()) * b.num_kv_heads * b.head_dim * elem * 2
+    qo = 2 * b.num_seqs * b.num_query_heads * b.head_dim * elem
+    tables = int(((ctx + b.block_size - 1) // b.block_size).sum()) * 4 + b.num_seqs * 4
+    write = b.num_seqs * b.num_kv_heads * b.head_dim * elem * 2 * 2 + b.num_seqs * 8
+    decode = kv + qo + tables
+    return decode + write, decode
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.strip().split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample_inputs(b, nseq, seed=1):
+    """Host copies (fp32 holding bf16-rounded N(0,1) values) of the first `nseq` sequences of the
+    batch, each as a compact cache with its own gather slots -- the shape of one reference call
+    per sequence, the way the reference's NativePagedBackend would be driven for decode."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    seqs = []
+    for s in range(nseq):
+        ctx = int(b.context_lens[s])
+        nb = -(-ctx // b.block_size)
+        shape = (1, nb, b.block_size, b.num_kv_heads, b.head_dim)
+        kc = O.bf16_bits_to_f32(O.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))).reshape(shape)
+        vc = O.bf16_bits_to_f32(O.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))).reshape(shape)
+        q = O.bf16_bits_to_f32(O.f32_to_bf16_bits(
+            rng.standard_normal((1, b.num_query_heads, 1, b.head_dim), dtype=np.float32))).reshape(
+            1, b.num_query_heads, 1, b.head_dim)
+        gs = np.arange(ctx, dtype=np.int32)
+        mask = np.ones((1, 1, 1, ctx), dtype=np.uint8)
+        seqs.append((q, kc, vc, gs, mask))
+    return seqs
+
+
+def run_cpu_kernel(b, seqs, repeats=1):
+    """Time the reference kernel (or the oracle port) over the sample; returns
+    (GB/s, seconds, kind, cores)."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    if O.RefKernel.available():
+        k = O.RefKernel()
+        k.set_threads(cores)
+        call, kind = k.paged_attention, "reference"
+    else:
+        os.environ["OMP_NUM_THREADS"] = str(cores)
+        call, kind = O.paged_attention, "port"
+    nbytes = 0
+    for q, kc, vc, gs, mask in seqs:
+        ctx = gs.shape[0]
+        nbytes += ctx * b.num_kv_heads * b.head_dim * 2 * 2 + 2 * b.num_query_heads * b.head_dim * 2
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        for q, kc, vc, gs, mask in seqs:
+            call(q, kc, vc, 0, gs, mask, b.scale)
+    dt = time.perf_counter() - t0
+    return nbytes * repeats / dt / 1e9, dt / repeats, kind, cores
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import __graft_entry__
+    wl = __graft_entry__.load_package().workloads
+    b = wl.config2(seed=0)
+    nseq = args.cpu_seqs
+    seqs = cpu_sample_inputs(b, nseq)
+    for _ in range(args.warmup):
+        run_cpu_kernel(b, seqs[:4])
+    vals, times = [], []
+    for _ in range(args.steps):
+        v, dt, kind, cores = run_cpu_kernel(b, seqs)
+        vals.append(v)
+        times.append(dt)
+    value = statistics.median(vals)
+    sample = (f"first {nseq} of the 256 config-2 sequences (sum ctx "
+              f"{int(b.context_lens[:nseq].sum())}), one reference call per sequence with bf16 "
+              f"values upcast to fp32, {kind} kernel")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(statistics.median(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 decode (256 seqs, GQA 32/8, D128, BS16), CPU sample",
+                   "seed": 0},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def ours_arm(args):
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200 import paged_ops
+    import llm_serving_b200._native as N
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if args.split:
+        N.lib().b200_set_decode_split_tokens(args.split)
+
+    b = pkg.workloads.config2(seed=rank, num_seqs=args.seqs)
+    total_bytes, decode_bytes = step_bytes(b)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    shape = (1, b.total_blocks, b.block_size, b.num_kv_heads, b.head_dim)
+    kc = torch.randn(shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    vc = torch.randn(shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    q = torch.randn((b.num_seqs, b.num_query_heads, b.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    newk = torch.randn((b.num_seqs, b.num_kv_heads, b.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    newv = torch.randn((b.num_seqs, b.num_kv_heads, b.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    slots = torch.from_numpy(b.slot_mapping()).to(dev)
+    bt = torch.from_numpy(b.block_tables()).to(dev)
+    ctx = torch.from_numpy(b.context_lens.astype(np.int32)).to(dev)
+    out = torch.empty_like(q)
+    max_ctx = int(b.context_lens.max())
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        paged_ops.reshape_and_cache(newk, newv, kc, vc, slots, 0)
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, b.scale, max_ctx, out=out)
+
+    launches_per_step = 3  # reshape_and_cache, decode plan, decode
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        paged_ops.reshape_and_cache(newk, newv, kc, vc, slots, 0)
+        ev[i][0].record(stream)
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, b.scale, max_ctx, out=out)
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+    decode_ms = sum(a.elapsed_time(c) for a, c in ev) / args.steps
+
+    # e2e through the public API with host buffers: H2D of the step's inputs, the kernels, D2H
+    # of the result, every step
+    h_q = q.cpu().pin_memory()
+    h_k = newk.cpu().pin_memory()
+    h_v = newv.cpu().pin_memory()
+    h_slots = slots.cpu().pin_memory()
+    h_bt = bt.cpu().pin_memory()
+    h_ctx = ctx.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_q, d_k, d_v = torch.empty_like(q), torch.empty_like(newk), torch.empty_like(newv)
+    d_slots, d_bt, d_ctx = torch.empty_like(slots), torch.empty_like(bt), torch.empty_like(ctx)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_bt, h_ctx))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_k.copy_(h_k, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        d_slots.copy_(h_slots, non_blocking=True)
+        d_bt.copy_(h_bt, non_blocking=True)
+        d_ctx.copy_(h_ctx, non_blocking=True)
+        paged_ops.reshape_and_cache(d_k, d_v, kc, vc, d_slots, 0)
+        paged_ops.paged_decode(d_q, kc, vc, 0, d_bt, d_ctx, b.scale, max_ctx, out=out)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+
+    times = torch.tensor([elapsed_ms, e2e_ms, decode_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms, decode_ms = times.tolist()
+    status = paged_ops.read_status(dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        seqs = cpu_sample_inputs(b, args.cpu_seqs)
+        v, dt, kind, cores = run_cpu_kernel(b, seqs)
+        cpu = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind,
+               "sample": f"first {args.cpu_seqs} config-2 sequences (sum ctx "
+                         f"{int(b.context_lens[:args.cpu_seqs].sum())}), one call per sequence, "
+                         f"bf16 values upcast to fp32; {dt:.2f} s"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = load_peaks()
+    ms_per_step = elapsed_ms / args.steps
+    value = world * total_bytes / (ms_per_step * 1e-3) / 1e9
+    achieved = decode_bytes / (decode_ms * 1e-3) / 1e9
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"config2 decode step: reshape_and_cache + paged decode, "
+                               f"{b.num_seqs} seqs/rank, ctx lognormal(1024,0.8) in [16,4096], "
+                               f"GQA 32/8, D 128, BS 16, bf16, shuffled pool",
+                   "sum_ctx_per_rank": int(b.context_lens.sum()),
+                   "bytes_per_step_per_rank": total_bytes,
+                   "l2": "inputs larger than L2 (KV ~%.2f GB per rank)" % (decode_bytes / 1e9),
+                   "parallelism": f"independent sequence shards x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": peak_kind,
+                     "kernel": "b200_paged_decode (plan + decode_tc), bytes per launch %d"
+                               % decode_bytes},
+        "e2e": {"value": round(world * total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9, 2),
+                "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "device_status": status,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seqs", type=int, default=256)
+    ap.add_argument("--split", type=int, default=0, help="decode split tokens (0 = heuristic)")
+    ap.add_argument("--cpu-seqs", type=int, default=32)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return ours_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

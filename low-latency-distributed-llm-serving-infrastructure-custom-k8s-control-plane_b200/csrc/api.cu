@@ -1,0 +1,496 @@
+// C ABI of libb200paged.so (include/b200_paged.h): argument validation, plans, tensor maps and
+// kernel launches.  No torch types; every entry point works on raw device pointers and a stream.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "attention.cuh"
+#include "cache_ops.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int cuda_fail(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return B200_ERR_CUDA;
+}
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int esize_of(int dtype) {
+  switch (dtype) {
+    case B200_DTYPE_F32: return 4;
+    case B200_DTYPE_BF16: return 2;
+    case B200_DTYPE_F16: return 2;
+    default: return 0;
+  }
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// ---- tensor maps -----------------------------------------------------------------------------
+// cuTensorMapEncodeTiled is fetched through the runtime's driver entry point, so the library
+// needs no link-time dependency on libcuda.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  int64_t rows;
+  int32_t chunks, box_rows, dtype, row_bytes;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && chunks == o.chunks && box_rows == o.box_rows &&
+           dtype == o.dtype && row_bytes == o.row_bytes;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.ptr) ^ (std::hash<int64_t>()(k.rows) * 31) ^
+           (static_cast<size_t>(k.chunks) << 20) ^ (static_cast<size_t>(k.box_rows) << 8);
+  }
+};
+
+// A paged cache (L, NB, BS, Hkv, D) of 2-byte elements viewed as a 3-D tensor:
+// dim0 = 64 elements (one 128-byte chunk of a head row), dim1 = Hkv * D/64 chunks of a token row,
+// dim2 = L*NB*BS token rows.  Box = (64, 1, box_rows), 128-byte swizzle.
+int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows,
+                     CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache_maps;
+  const int64_t rows = static_cast<int64_t>(g.num_layers) * g.total_blocks * g.block_size;
+  const int chunks = g.num_kv_heads * (g.head_dim / 64);
+  const int row_bytes = g.num_kv_heads * g.head_dim * 2;
+  MapKey key{cache, rows, chunks, box_rows, g.dtype, row_bytes};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache_maps.find(key);
+  if (it != cache_maps.end()) {
+    *out = it->second;
+    return B200_OK;
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(cache) % 16 != 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "cache pointer must be 16-byte aligned");
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(chunks), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = g.dtype == B200_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(&m, dt, 3, const_cast<void*>(cache), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  if (cache_maps.size() > 256) cache_maps.clear();
+  cache_maps.emplace(key, m);
+  *out = m;
+  return B200_OK;
+}
+
+int g_split_override = 0;
+
+struct DecodePlan {
+  bool tensor_cores;
+  int split_tokens;
+  int nchunks, hpc, items_per_split;
+  int64_t max_splits;
+  size_t off_cu, off_work, off_cnt, off_lse, off_o, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+int validate_geom(const B200CacheGeometry& g, int32_t layer_idx, int32_t hq) {
+  if (esize_of(g.dtype) == 0) return fail(B200_ERR_UNSUPPORTED, "unsupported dtype");
+  if (g.num_layers <= 0 || g.total_blocks <= 0 || g.block_size <= 0 || g.num_kv_heads <= 0 ||
+      g.head_dim <= 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "cache geometry must be positive");
+  if (hq <= 0 || hq % g.num_kv_heads != 0)
+    return fail(B200_ERR_INVALID_ARGUMENT,
+                "num_query_heads must be a multiple of num_kv_heads for GQA");
+  if (layer_idx < 0 || layer_idx >= g.num_layers)
+    return fail(B200_ERR_INVALID_ARGUMENT, "layer_idx out of range");
+  if (g.head_dim > 256) return fail(B200_ERR_UNSUPPORTED, "head_dim > 256");
+  return B200_OK;
+}
+
+bool tc_eligible(const B200CacheGeometry& g, const void* q, int64_t qs_row, int64_t qs_head,
+                 const void* kc, const void* vc) {
+  if (g.dtype != B200_DTYPE_BF16 && g.dtype != B200_DTYPE_F16) return false;
+  if (g.head_dim != 64 && g.head_dim != 128) return false;
+  if (!(g.block_size == 8 || g.block_size % 16 == 0)) return false;
+  if (reinterpret_cast<uintptr_t>(q) % 4 != 0 || (qs_row & 1) || (qs_head & 1)) return false;
+  if (reinterpret_cast<uintptr_t>(kc) % 16 != 0 || reinterpret_cast<uintptr_t>(vc) % 16 != 0)
+    return false;
+  const int64_t rows = static_cast<int64_t>(g.num_layers) * g.total_blocks * g.block_size;
+  if (rows >= (int64_t(1) << 31)) return false;
+  return true;
+}
+
+DecodePlan make_decode_plan(const B200DecodeParams& p) {
+  DecodePlan pl{};
+  const int G = p.num_query_heads / p.geom.num_kv_heads;
+  pl.tensor_cores = tc_eligible(p.geom, p.query, p.q_stride_row, p.q_stride_head, p.key_cache,
+                                p.value_cache);
+  pl.nchunks = (G + 7) / 8;
+  pl.hpc = G < 8 ? G : 8;
+  pl.items_per_split = p.geom.num_kv_heads * pl.nchunks;
+  const int64_t max_ctx = p.max_context_len > 0 ? p.max_context_len : 1;
+  int split = g_split_override;
+  if (split <= 0) {
+    split = 512;
+    while (split > 64 &&
+           static_cast<int64_t>(p.num_seqs) * ((max_ctx + split - 1) / split) * pl.items_per_split <
+               4LL * num_sms())
+      split /= 2;
+  }
+  pl.split_tokens = split;
+  pl.max_splits = static_cast<int64_t>(p.num_seqs) * ((max_ctx + split - 1) / split);
+  size_t off = align256(sizeof(b200::DecodeHeader));
+  pl.off_cu = off;
+  off += align256((p.num_seqs + 1) * sizeof(int32_t));
+  pl.off_work = off;
+  off += align256(pl.max_splits * sizeof(int2));
+  pl.off_cnt = off;
+  off += align256(static_cast<size_t>(p.num_seqs) * pl.items_per_split * sizeof(int32_t));
+  pl.off_lse = off;
+  off += align256(static_cast<size_t>(pl.max_splits) * pl.items_per_split * pl.hpc * 4);
+  pl.off_o = off;
+  off += align256(static_cast<size_t>(pl.max_splits) * pl.items_per_split * pl.hpc *
+                  p.geom.head_dim * 4);
+  pl.total = pl.tensor_cores ? off : 0;
+  return pl;
+}
+
+}  // namespace
+
+namespace b200 {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace b200
+
+extern "C" {
+
+const char* b200_status_string(int status) {
+  switch (status) {
+    case B200_OK: return "ok";
+    case B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case B200_ERR_OUT_OF_MEMORY: return "out of memory";
+    case B200_ERR_OUT_OF_RANGE: return "out of range";
+    case B200_ERR_RUNTIME: return "runtime error";
+    case B200_ERR_UNSUPPORTED: return "unsupported";
+    case B200_ERR_CUDA: return "cuda error";
+    default: return "unknown status";
+  }
+}
+
+const char* b200_last_error(void) { return g_last_error.c_str(); }
+
+void b200_set_decode_split_tokens(int32_t tokens) {
+  g_split_override = tokens > 0 ? ((tokens + 15) / 16) * 16 : 0;
+}
+
+// ---- reference-signature masked attention ---------------------------------------------------
+
+int b200_paged_attention(const float* query, const float* key_cache, const float* value_cache,
+                         int32_t layer_idx, PagedAttentionDims dims, const int32_t* gather_slots,
+                         const uint8_t* attention_mask, float scaling, float* output,
+                         int32_t* status_word, void* stream) {
+  B200CacheGeometry g{dims.num_layers, dims.total_blocks, dims.block_size, dims.num_kv_heads,
+                      dims.head_dim, B200_DTYPE_F32};
+  int rc = validate_geom(g, layer_idx, dims.num_query_heads);
+  if (rc != B200_OK) return rc;
+  if (dims.num_query_tokens < 0 || dims.num_context_tokens < 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "negative token counts");
+  if (dims.num_query_tokens == 0) return B200_OK;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = dims.num_query_heads / dims.num_kv_heads;
+  b200::RowArgs a{};
+  a.mode = b200::kRowMask;
+  a.q = query;
+  a.q_srow = dims.head_dim;
+  a.q_shead = static_cast<int64_t>(dims.num_query_tokens) * dims.head_dim;
+  a.kc = key_cache;
+  a.vc = value_cache;
+  a.layer = layer_idx;
+  a.nb = dims.total_blocks;
+  a.bs = dims.block_size;
+  a.hkv = dims.num_kv_heads;
+  a.head_dim = dims.head_dim;
+  a.group = G;
+  a.nchunks = (G + 7) / 8;
+  a.gather = gather_slots;
+  a.mask = attention_mask;
+  a.num_ctx = dims.num_context_tokens;
+  a.scale = scaling;
+  a.out = output;
+  a.o_srow = static_cast<int64_t>(dims.num_query_heads) * dims.head_dim;
+  a.o_shead = dims.head_dim;
+  a.status = status_word;
+  cudaError_t e = b200::launch_row(B200_DTYPE_F32, a, dims.num_query_tokens, st);
+  if (e != cudaSuccess) return cuda_fail(e, "paged_attention");
+  return B200_OK;
+}
+
+void paged_attention(const float* query, const float* key_cache, const float* value_cache,
+                     const int32_t layer_idx, const PagedAttentionDims dims,
+                     const int32_t* gather_slots, const uint8_t* attention_mask,
+                     const float scaling, float* output, float* scratch, void* stream) {
+  (void)scratch;
+  b200_paged_attention(query, key_cache, value_cache, layer_idx, dims, gather_slots,
+                       attention_mask, scaling, output, nullptr, stream);
+}
+
+// ---- decode ---------------------------------------------------------------------------------
+
+size_t b200_paged_decode_workspace_bytes(const B200DecodeParams* p) {
+  if (p == nullptr || p->num_seqs <= 0 || p->geom.num_kv_heads <= 0 ||
+      p->num_query_heads % p->geom.num_kv_heads != 0)
+    return 0;
+  return make_decode_plan(*p).total;
+}
+
+int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
+  const B200DecodeParams& p = *pp;
+  int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
+  if (rc != B200_OK) return rc;
+  if (p.num_seqs < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_seqs < 0");
+  if (p.num_seqs == 0) return B200_OK;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = p.num_query_heads / p.geom.num_kv_heads;
+  const DecodePlan pl = make_decode_plan(p);
+  if (!pl.tensor_cores) {
+    b200::RowArgs a{};
+    a.mode = b200::kRowBlockTable;
+    a.q = p.query;
+    a.q_srow = p.q_stride_row;
+    a.q_shead = p.q_stride_head;
+    a.query_rows = p.query_rows;
+    a.kc = p.key_cache;
+    a.vc = p.value_cache;
+    a.layer = p.layer_idx;
+    a.nb = p.geom.total_blocks;
+    a.bs = p.geom.block_size;
+    a.hkv = p.geom.num_kv_heads;
+    a.head_dim = p.geom.head_dim;
+    a.group = G;
+    a.nchunks = (G + 7) / 8;
+    a.bt = p.block_tables;
+    a.bt_stride = p.block_table_stride;
+    a.ctx_lens = p.context_lens;
+    a.cu_q = nullptr;
+    a.S = p.num_seqs;
+    a.scale = p.scale;
+    a.out = p.out;
+    a.o_srow = p.o_stride_row;
+    a.o_shead = p.o_stride_head;
+    a.status = p.status_word;
+    cudaError_t e = b200::launch_row(p.geom.dtype, a, p.num_seqs, st);
+    if (e != cudaSuccess) return cuda_fail(e, "paged_decode(row)");
+    return B200_OK;
+  }
+  if (workspace == nullptr || workspace_bytes < pl.total)
+    return fail(B200_ERR_INVALID_ARGUMENT, "decode workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "decode workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  auto* hdr = reinterpret_cast<b200::DecodeHeader*>(ws);
+  auto* cu = reinterpret_cast<int32_t*>(ws + pl.off_cu);
+  auto* work = reinterpret_cast<int2*>(ws + pl.off_work);
+  auto* cnt = reinterpret_cast<int32_t*>(ws + pl.off_cnt);
+  auto* lse = reinterpret_cast<float*>(ws + pl.off_lse);
+  auto* po = reinterpret_cast<float*>(ws + pl.off_o);
+
+  CUtensorMap km, vm;
+  const int box_rows = p.geom.block_size >= 16 ? 16 : 8;
+  rc = cache_tensor_map(p.key_cache, p.geom, box_rows, &km);
+  if (rc != B200_OK) return rc;
+  rc = cache_tensor_map(p.value_cache, p.geom, box_rows, &vm);
+  if (rc != B200_OK) return rc;
+
+  b200::PlanArgs pa{};
+  pa.ctx_lens = p.context_lens;
+  pa.query_rows = p.query_rows;
+  pa.S = p.num_seqs;
+  pa.max_ctx = p.max_context_len;
+  pa.split_tokens = pl.split_tokens;
+  pa.items_per_split = pl.items_per_split;
+  pa.hq = p.num_query_heads;
+  pa.head_dim = p.geom.head_dim;
+  pa.esize = esize_of(p.geom.dtype);
+  pa.o_srow = p.o_stride_row;
+  pa.o_shead = p.o_stride_head;
+  pa.out = p.out;
+  pa.status = p.status_word;
+  pa.hdr = hdr;
+  pa.cu_splits = cu;
+  pa.work_sp = work;
+  pa.counters = cnt;
+  cudaError_t e = b200::launch_plan(pa, st);
+  if (e != cudaSuccess) return cuda_fail(e, "decode plan");
+
+  b200::DecodeArgs a{};
+  a.q = p.query;
+  a.q_srow = p.q_stride_row;
+  a.q_shead = p.q_stride_head;
+  a.query_rows = p.query_rows;
+  a.layer = p.layer_idx;
+  a.nb = p.geom.total_blocks;
+  a.bs = p.geom.block_size;
+  a.hkv = p.geom.num_kv_heads;
+  a.hq = p.num_query_heads;
+  a.group = G;
+  a.nchunks = pl.nchunks;
+  a.hpc = pl.hpc;
+  a.bt = p.block_tables;
+  a.bt_stride = p.block_table_stride;
+  a.ctx_lens = p.context_lens;
+  a.S = p.num_seqs;
+  a.max_ctx = p.max_context_len;
+  a.split_tokens = pl.split_tokens;
+  a.scale_log2 = p.scale * b200::kLog2e;
+  a.out = p.out;
+  a.o_srow = p.o_stride_row;
+  a.o_shead = p.o_stride_head;
+  a.status = p.status_word;
+  a.hdr = hdr;
+  a.cu_splits = cu;
+  a.work_sp = work;
+  a.counters = cnt;
+  a.part_lse = lse;
+  a.part_o = po;
+  const int64_t max_items = pl.max_splits * pl.items_per_split;
+  e = b200::launch_decode_tc(p.geom.dtype, p.geom.head_dim, km, vm, a,
+                             static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30)), st);
+  if (e != cudaSuccess) return cuda_fail(e, "decode");
+  return B200_OK;
+}
+
+// ---- prefill (ragged causal) ----------------------------------------------------------------
+
+size_t b200_paged_prefill_workspace_bytes(const B200PrefillParams* p) {
+  (void)p;
+  return 0;
+}
+
+int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
+  const B200PrefillParams& p = *pp;
+  int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
+  if (rc != B200_OK) return rc;
+  if (p.num_seqs < 0 || p.num_tokens < 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "negative sizes");
+  if (p.num_seqs == 0 || p.num_tokens == 0) return B200_OK;
+  const int G = p.num_query_heads / p.geom.num_kv_heads;
+  b200::RowArgs a{};
+  a.mode = b200::kRowBlockTable;
+  a.q = p.query;
+  a.q_srow = p.q_stride_token;
+  a.q_shead = p.q_stride_head;
+  a.kc = p.key_cache;
+  a.vc = p.value_cache;
+  a.layer = p.layer_idx;
+  a.nb = p.geom.total_blocks;
+  a.bs = p.geom.block_size;
+  a.hkv = p.geom.num_kv_heads;
+  a.head_dim = p.geom.head_dim;
+  a.group = G;
+  a.nchunks = (G + 7) / 8;
+  a.bt = p.block_tables;
+  a.bt_stride = p.block_table_stride;
+  a.ctx_lens = p.context_lens;
+  a.cu_q = p.cu_seqlens;
+  a.S = p.num_seqs;
+  a.scale = p.scale;
+  a.out = p.out;
+  a.o_srow = p.o_stride_token;
+  a.o_shead = p.o_stride_head;
+  a.status = p.status_word;
+  cudaError_t e = b200::launch_row(p.geom.dtype, a, p.num_tokens, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged_prefill(row)");
+  return B200_OK;
+}
+
+// ---- reshape_and_cache ------------------------------------------------------------------------
+
+int b200_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_stride_head,
+                           const void* value, int64_t v_stride_token, int64_t v_stride_head,
+                           void* key_cache, void* value_cache, const B200CacheGeometry* geom,
+                           int32_t layer_idx, const int64_t* slot_mapping, int32_t num_tokens,
+                           int32_t* status_word, void* stream) {
+  if (geom == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null geometry");
+  const B200CacheGeometry& g = *geom;
+  const int es = esize_of(g.dtype);
+  if (es == 0) return fail(B200_ERR_UNSUPPORTED, "unsupported dtype");
+  if (layer_idx < 0 || layer_idx >= g.num_layers)
+    return fail(B200_ERR_INVALID_ARGUMENT, "layer_idx out of range");
+  if (num_tokens < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_tokens < 0");
+  if (num_tokens == 0) return B200_OK;
+  b200::CacheWriteArgs a{};
+  a.key = key;
+  a.value = value;
+  a.k_stok = k_stride_token * es;
+  a.k_shead = k_stride_head * es;
+  a.v_stok = v_stride_token * es;
+  a.v_shead = v_stride_head * es;
+  a.kc = key_cache;
+  a.vc = value_cache;
+  a.layer = layer_idx;
+  a.nb = g.total_blocks;
+  a.bs = g.block_size;
+  a.hkv = g.num_kv_heads;
+  a.head_bytes = static_cast<int64_t>(g.head_dim) * es;
+  a.slots = slot_mapping;
+  a.num_tokens = num_tokens;
+  a.status = status_word;
+  // widest vector that divides every address and stride
+  uint64_t align = static_cast<uint64_t>(a.head_bytes) | static_cast<uint64_t>(a.k_stok) |
+                   static_cast<uint64_t>(a.k_shead) | static_cast<uint64_t>(a.v_stok) |
+                   static_cast<uint64_t>(a.v_shead) | reinterpret_cast<uintptr_t>(key) |
+                   reinterpret_cast<uintptr_t>(value) | reinterpret_cast<uintptr_t>(key_cache) |
+                   reinterpret_cast<uintptr_t>(value_cache);
+  int vec = 16;
+  while (vec > 2 && (align % vec) != 0) vec /= 2;
+  if (align % vec != 0) return fail(B200_ERR_INVALID_ARGUMENT, "misaligned key/value rows");
+  cudaError_t e = b200::launch_reshape_and_cache(a, vec, num_sms(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "reshape_and_cache");
+  return B200_OK;
+}
+
+}  // extern "C"

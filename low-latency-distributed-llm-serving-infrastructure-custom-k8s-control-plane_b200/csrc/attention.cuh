@@ -1,0 +1,101 @@
+// Internal interface between the attention kernels (attention.cu) and the C ABI (api.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace b200 {
+
+constexpr int kDecodeWarps = 4;
+constexpr int kDecodeThreads = 32 * kDecodeWarps;
+constexpr int kDecodeStages = 2;  // TMA ring depth per warp (2 CTAs per SM fit)
+
+// Shared-memory tile of one 16-token unit: K then V, each D/64 sub-buffers of 16 rows x 128 B
+// (128B-swizzled, as TMA writes them).
+template <int D>
+struct TcTile {
+  static constexpr int kSub = D / 64;
+  static constexpr int kHalf = 16 * D * 2;  // bytes of the K (or V) tile
+  static constexpr int kStage = 2 * kHalf;
+};
+
+struct DecodeHeader {
+  int32_t total_items;
+  int32_t next_item;
+  int32_t total_splits;
+  int32_t pad;
+};
+
+struct PlanArgs {
+  const int32_t* ctx_lens;
+  const int32_t* query_rows;
+  int32_t S;
+  int32_t max_ctx;
+  int32_t split_tokens;
+  int32_t items_per_split;
+  int32_t hq;
+  int32_t head_dim;
+  int32_t esize;
+  int64_t o_srow, o_shead;
+  void* out;
+  int32_t* status;
+  DecodeHeader* hdr;
+  int32_t* cu_splits;
+  int2* work_sp;
+  int32_t* counters;
+};
+
+struct DecodeArgs {
+  const void* q;
+  int64_t q_srow, q_shead;
+  const int32_t* query_rows;
+  int32_t layer, nb, bs, hkv, hq, group, nchunks, hpc;
+  const int32_t* bt;
+  int32_t bt_stride;
+  const int32_t* ctx_lens;
+  int32_t S;
+  int32_t max_ctx;
+  int32_t split_tokens;
+  float scale_log2;
+  void* out;
+  int64_t o_srow, o_shead;
+  int32_t* status;
+  DecodeHeader* hdr;
+  const int32_t* cu_splits;
+  const int2* work_sp;
+  int32_t* counters;
+  float* part_lse;
+  float* part_o;
+};
+
+enum RowMode : int32_t { kRowBlockTable = 0, kRowMask = 1 };
+
+struct RowArgs {
+  int32_t mode;
+  const void* q;
+  int64_t q_srow, q_shead;
+  const int32_t* query_rows;
+  const void* kc;
+  const void* vc;
+  int32_t layer, nb, bs, hkv, head_dim, group, nchunks;
+  // block-table mode
+  const int32_t* bt;
+  int32_t bt_stride;
+  const int32_t* ctx_lens;
+  const int64_t* cu_q;  // NULL: one row per sequence (decode)
+  int32_t S;
+  // mask mode
+  const int32_t* gather;
+  const uint8_t* mask;
+  int32_t num_ctx;
+  float scale;
+  void* out;
+  int64_t o_srow, o_shead;
+  int32_t* status;
+};
+
+cudaError_t launch_plan(const PlanArgs& a, cudaStream_t stream);
+cudaError_t launch_decode_tc(int dtype, int head_dim, const CUtensorMap& km, const CUtensorMap& vm,
+                             const DecodeArgs& a, int max_items, cudaStream_t stream);
+cudaError_t launch_row(int dtype, const RowArgs& a, int rows, cudaStream_t stream);
+
+}  // namespace b200

@@ -1,0 +1,191 @@
+"""Drop-in for the reference's pybind module ``llm_allocator_cpp`` (csrc/src/bindings.cpp:79-117).
+
+* ``PageAllocator``      -- the host C++ allocator in libb200paged.so (b200_host_*), with the
+                            reference's FIFO / refcount / swap semantics and exception types
+                            (csrc/include/page_allocator.hpp:45-374).
+* ``SequenceBlockTable`` -- per-sequence block list over a PageAllocator
+                            (page_allocator.hpp:376-475); keeps its allocator alive.
+* ``paged_attention``    -- the reference kernel's contract (bindings.cpp:10-76) executed by the
+                            B200 kernel behind the C symbol ``paged_attention``.  CUDA tensors in
+                            -> CUDA tensor out, with no copies; numpy arrays or CPU tensors are
+                            copied to the GPU and the result is returned as numpy, as the
+                            reference returns it.  There is no CPU execution path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List
+
+from . import _native as N
+
+
+def _chk(rc: int) -> None:
+    N.check(rc, host_message=True)
+
+
+class PageAllocator:
+    def __init__(self, total_blocks: int, tokens_per_block: int, bytes_per_token: int,
+                 total_cpu_blocks: int = 32) -> None:
+        for v in (total_blocks, tokens_per_block, bytes_per_token, total_cpu_blocks):
+            if int(v) < 0:  # size_t arguments in the reference binding
+                raise TypeError("incompatible constructor arguments (negative size)")
+        h = ctypes.c_void_p()
+        _chk(N.lib().b200_host_allocator_create(int(total_blocks), int(tokens_per_block),
+                                                int(bytes_per_token), int(total_cpu_blocks),
+                                                ctypes.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            N.lib().b200_host_allocator_destroy(h)
+            self._h = None
+
+    def allocate_block(self) -> int:
+        out = ctypes.c_int32()
+        _chk(N.lib().b200_host_allocate_block(self._h, ctypes.byref(out)))
+        return out.value
+
+    def allocate_blocks(self, count: int) -> List[int]:
+        if int(count) < 0:
+            raise TypeError("count must be non-negative")
+        buf = (ctypes.c_int32 * max(1, int(count)))()
+        _chk(N.lib().b200_host_allocate_blocks(self._h, int(count), buf))
+        return list(buf[:int(count)])
+
+    def share_block(self, block_id: int) -> None:
+        _chk(N.lib().b200_host_share_block(self._h, int(block_id)))
+
+    def free_block(self, block_id: int) -> None:
+        _chk(N.lib().b200_host_free_block(self._h, int(block_id)))
+
+    def swap_out(self, gpu_block_id: int) -> int:
+        out = ctypes.c_int32()
+        _chk(N.lib().b200_host_swap_out(self._h, int(gpu_block_id), ctypes.byref(out)))
+        return out.value
+
+    def swap_in(self, cpu_block_id: int) -> int:
+        out = ctypes.c_int32()
+        _chk(N.lib().b200_host_swap_in(self._h, int(cpu_block_id), ctypes.byref(out)))
+        return out.value
+
+    def get_cpu_block_id(self, gpu_block_id: int) -> int:
+        out = ctypes.c_int32()
+        _chk(N.lib().b200_host_get_cpu_block_id(self._h, int(gpu_block_id), ctypes.byref(out)))
+        return out.value
+
+    def release_swapped_block(self, cpu_block_id: int) -> None:
+        _chk(N.lib().b200_host_release_swapped_block(self._h, int(cpu_block_id)))
+
+    def get_host_ptr(self, cpu_block_id: int) -> int:
+        out = ctypes.c_uint64()
+        _chk(N.lib().b200_host_get_host_ptr(self._h, int(cpu_block_id), ctypes.byref(out)))
+        return out.value
+
+    def get_device_ptr(self, gpu_block_id: int) -> int:
+        out = ctypes.c_uint64()
+        _chk(N.lib().b200_host_get_device_ptr(self._h, int(gpu_block_id), ctypes.byref(out)))
+        return out.value
+
+    def is_zero_copy(self) -> bool:
+        # host swap pool in plain host memory, as the reference's CPU memory backend
+        return True
+
+    def get_block_size(self) -> int:
+        return int(N.lib().b200_host_block_size(self._h))
+
+    def get_bytes_per_token(self) -> int:
+        return int(N.lib().b200_host_bytes_per_token(self._h))
+
+    def get_host_pool_bytes(self) -> int:
+        return int(N.lib().b200_host_pool_bytes(self._h))
+
+    def get_num_free_blocks(self) -> int:
+        return int(N.lib().b200_host_num_free_blocks(self._h))
+
+    def get_num_free_cpu_blocks(self) -> int:
+        return int(N.lib().b200_host_num_free_cpu_blocks(self._h))
+
+    def get_total_blocks(self) -> int:
+        return int(N.lib().b200_host_total_blocks(self._h))
+
+    def get_utilization_percentage(self) -> float:
+        return float(N.lib().b200_host_utilization(self._h))
+
+
+class SequenceBlockTable:
+    """append_token allocates a block whenever the token count is a multiple of the block size
+    (page_allocator.hpp:426-434); release frees in table order (:461-469)."""
+
+    def __init__(self, allocator: PageAllocator) -> None:
+        self._allocator = allocator  # keep-alive, as py::keep_alive<1, 2> in the reference
+        self._block_size = allocator.get_block_size()
+        self._blocks: List[int] = []
+        self._tokens = 0
+
+    def append_token(self) -> None:
+        if self._tokens % self._block_size == 0:
+            self._blocks.append(self._allocator.allocate_block())
+        self._tokens += 1
+
+    def append_tokens(self, n: int) -> None:
+        """n x append_token, with one allocator call for the whole run of new blocks when they
+        fit (same blocks and same partial result on OOM as the token-by-token loop)."""
+        n = int(n)
+        bs = self._block_size
+        need = (self._tokens + n + bs - 1) // bs - (self._tokens + bs - 1) // bs
+        if need <= self._allocator.get_num_free_blocks():
+            if need:
+                self._blocks.extend(self._allocator.allocate_blocks(need))
+            self._tokens += n
+            return
+        for _ in range(n):
+            self.append_token()
+
+    def append_block(self, block_id: int) -> None:
+        if int(block_id) < 0 or int(block_id) >= self._allocator.get_total_blocks():
+            raise IndexError(f"Block ID out of range: {int(block_id)}")
+        self._blocks.append(int(block_id))
+
+    def replace_block(self, old_block_id: int, new_block_id: int) -> None:
+        if int(new_block_id) < 0 or int(new_block_id) >= self._allocator.get_total_blocks():
+            raise IndexError(f"Block ID out of range: {int(new_block_id)}")
+        try:
+            i = self._blocks.index(int(old_block_id))
+        except ValueError:
+            raise RuntimeError(f"Block ID {int(old_block_id)} not found in block table") from None
+        self._blocks[i] = int(new_block_id)
+
+    def release(self) -> None:
+        for b in self._blocks:
+            self._allocator.free_block(b)
+        self._blocks = []
+        self._tokens = 0
+
+    def get_physical_blocks(self) -> List[int]:
+        return list(self._blocks)
+
+    def get_tokens_count(self) -> int:
+        return self._tokens
+
+
+def paged_attention(query, key_cache, value_cache, layer_idx, gather_slots, attention_mask,
+                    scaling):
+    """The reference binding's contract (bindings.cpp:10-76) on the B200 kernel."""
+    import numpy as np
+    import torch
+
+    from .paged_ops import paged_attention_masked
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("paged_attention runs on the GPU; no CUDA device is available")
+    args = [query, key_cache, value_cache, gather_slots, attention_mask]
+    on_device = all(isinstance(a, torch.Tensor) and a.is_cuda for a in args)
+    dev = next((a.device for a in args if isinstance(a, torch.Tensor) and a.is_cuda),
+               torch.device("cuda"))
+    t = [a.to(dev) if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+         for a in args]
+    out = paged_attention_masked(t[0], t[1], t[2], int(layer_idx), t[3], t[4], float(scaling))
+    if on_device:
+        return out
+    return out.cpu().numpy()

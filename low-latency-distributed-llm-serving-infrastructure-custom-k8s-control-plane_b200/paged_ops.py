@@ -1,0 +1,218 @@
+"""Torch-tensor front end of the C ABI: device tensors in, device tensors out.
+
+torch is used here for device memory and streams only; every computation runs in
+libb200paged.so.  Each function raises if a tensor is not on a CUDA device -- there is no CPU
+fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.DTYPE_F32, torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_F16}
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("libb200paged kernels need CUDA tensors (no CPU fallback)")
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def cache_geometry(key_cache: torch.Tensor) -> N.CacheGeometry:
+    if key_cache.dim() != 5:
+        raise ValueError("key_cache must be 5-D (layers, blocks, block_size, heads, dim)")
+    if not key_cache.is_contiguous():
+        raise ValueError("caches must be contiguous (L, NB, BS, Hkv, D)")
+    if key_cache.dtype not in _DTYPES:
+        raise ValueError(f"unsupported cache dtype {key_cache.dtype}")
+    L, NB, BS, Hkv, D = key_cache.shape
+    return N.CacheGeometry(L, NB, BS, Hkv, D, _DTYPES[key_cache.dtype])
+
+
+class Workspace:
+    """Grow-only device scratch buffer per device (256-byte aligned)."""
+
+    def __init__(self):
+        self._buf = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.type, device.index)
+        buf = self._buf.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self._buf[key] = buf
+        return buf
+
+
+_WORKSPACE = Workspace()
+_STATUS = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    key = (device.type, device.index)
+    if key not in _STATUS:
+        _STATUS[key] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _STATUS[key]
+
+
+def read_status(device: torch.device, reset: bool = True) -> int:
+    s = status_word(device)
+    v = int(s.item())
+    if reset:
+        s.zero_()
+    return v
+
+
+def decode_params(query, key_cache, value_cache, layer_idx, block_tables, context_lens, scale,
+                  out, max_context_len, query_rows=None, status=None) -> N.DecodeParams:
+    geom = cache_geometry(key_cache)
+    if query.dim() != 3 or query.stride(-1) != 1:
+        raise ValueError("query must be (rows, Hq, D) with the head dim contiguous")
+    if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
+        raise ValueError("block_tables and context_lens must be int32")
+    p = N.DecodeParams()
+    p.query = query.data_ptr()
+    p.q_stride_row, p.q_stride_head = query.stride(0), query.stride(1)
+    p.query_rows = _ptr(query_rows)
+    p.key_cache, p.value_cache = key_cache.data_ptr(), value_cache.data_ptr()
+    p.geom = geom
+    p.layer_idx = int(layer_idx)
+    p.num_query_heads = query.shape[1]
+    p.block_tables = block_tables.data_ptr()
+    p.block_table_stride = block_tables.stride(0) if block_tables.dim() == 2 else 0
+    p.context_lens = context_lens.data_ptr()
+    p.num_seqs = context_lens.shape[0]
+    p.max_context_len = int(max_context_len)
+    p.scale = float(scale)
+    p.out = out.data_ptr()
+    p.o_stride_row, p.o_stride_head = out.stride(0), out.stride(1)
+    p.status_word = _ptr(status)
+    return p
+
+
+def paged_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                 layer_idx: int, block_tables: torch.Tensor, context_lens: torch.Tensor,
+                 scale: float, max_context_len: int, out: Optional[torch.Tensor] = None,
+                 query_rows: Optional[torch.Tensor] = None,
+                 workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode attention (one new token per sequence) read through block tables (K1).
+    query (rows, Hq, D); caches (L, NB, BS, Hkv, D); block_tables (S, max_blocks) int32;
+    context_lens (S,) int32.  Returns out (rows, Hq, D) in the cache dtype."""
+    _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
+    if out is None:
+        out = torch.empty_like(query, dtype=key_cache.dtype)
+    st = status_word(query.device)
+    p = decode_params(query, key_cache, value_cache, layer_idx, block_tables, context_lens, scale,
+                      out, max_context_len, query_rows, st)
+    L = N.lib()
+    need = L.b200_paged_decode_workspace_bytes(ctypes.byref(p))
+    ws = workspace if workspace is not None else _WORKSPACE.get(query.device, need)
+    N.check(L.b200_paged_decode(ctypes.byref(p), ws.data_ptr() if need else None, ws.numel(),
+                                _stream(query.device)))
+    return out
+
+
+def paged_prefill(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                  layer_idx: int, block_tables: torch.Tensor, cu_seqlens: torch.Tensor,
+                  context_lens: torch.Tensor, scale: float, max_query_len: int,
+                  max_context_len: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Ragged causal attention through block tables (prefill chunks / mixed steps).
+    query (Ntok, Hq, D); cu_seqlens (S+1,) int64; context_lens (S,) int32."""
+    _require_cuda(query, key_cache, value_cache, block_tables, cu_seqlens, context_lens)
+    if out is None:
+        out = torch.empty_like(query, dtype=key_cache.dtype)
+    geom = cache_geometry(key_cache)
+    p = N.PrefillParams()
+    p.query = query.data_ptr()
+    p.q_stride_token, p.q_stride_head = query.stride(0), query.stride(1)
+    p.key_cache, p.value_cache = key_cache.data_ptr(), value_cache.data_ptr()
+    p.geom = geom
+    p.layer_idx = int(layer_idx)
+    p.num_query_heads = query.shape[1]
+    p.block_tables = block_tables.data_ptr()
+    p.block_table_stride = block_tables.stride(0)
+    p.cu_seqlens = cu_seqlens.data_ptr()
+    p.context_lens = context_lens.data_ptr()
+    p.num_seqs = context_lens.shape[0]
+    p.num_tokens = query.shape[0]
+    p.max_query_len = int(max_query_len)
+    p.max_context_len = int(max_context_len)
+    p.scale = float(scale)
+    p.out = out.data_ptr()
+    p.o_stride_token, p.o_stride_head = out.stride(0), out.stride(1)
+    p.status_word = status_word(query.device).data_ptr()
+    L = N.lib()
+    need = L.b200_paged_prefill_workspace_bytes(ctypes.byref(p))
+    ws = _WORKSPACE.get(query.device, need) if need else None
+    N.check(L.b200_paged_prefill(ctypes.byref(p), None if ws is None else ws.data_ptr(),
+                                 0 if ws is None else ws.numel(), _stream(query.device)))
+    return out
+
+
+def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
+                      value_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                      layer_idx: int) -> None:
+    """key/value (Ntok, Hkv, D) (any strides, D contiguous) -> cache slots (K2)."""
+    _require_cuda(key, value, key_cache, value_cache, slot_mapping)
+    geom = cache_geometry(key_cache)
+    if key.dtype != key_cache.dtype or value.dtype != value_cache.dtype:
+        raise ValueError("key/value dtype must match the cache dtype")
+    if slot_mapping.dtype != torch.int64:
+        raise ValueError("slot_mapping must be int64")
+    if key.stride(-1) != 1 or value.stride(-1) != 1:
+        raise ValueError("head dim must be contiguous")
+    N.check(N.lib().b200_reshape_and_cache(
+        key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(), value.stride(0),
+        value.stride(1), key_cache.data_ptr(), value_cache.data_ptr(), ctypes.byref(geom),
+        int(layer_idx), slot_mapping.data_ptr(), slot_mapping.numel(),
+        status_word(key.device).data_ptr(), _stream(key.device)))
+
+
+def paged_attention_masked(query: torch.Tensor, key_cache: torch.Tensor,
+                           value_cache: torch.Tensor, layer_idx: int, gather_slots: torch.Tensor,
+                           attention_mask: torch.Tensor, scaling: float) -> torch.Tensor:
+    """The reference kernel's own contract (csrc/src/bindings.cpp:10-76) on the device:
+    query (1,Hq,Nq,D) fp32, caches fp32, gather_slots (Nctx,) int32, mask (1,1,Nq,Nctx)
+    -> (1,Nq,Hq,D) fp32, through the C symbol `paged_attention`."""
+    _require_cuda(query, key_cache, value_cache, gather_slots, attention_mask)
+    if query.dim() != 4:
+        raise RuntimeError("query must be 4-D (1, heads, seq, dim)")
+    if key_cache.dim() != 5:
+        raise RuntimeError("key_cache must be 5-D (layers, blocks, block_size, heads, dim)")
+    if gather_slots.dim() != 1:
+        raise RuntimeError("gather_slots must be 1-D")
+    if attention_mask.dim() != 4:
+        raise RuntimeError("attention_mask must be 4-D (1, 1, query, context)")
+    q = query.to(torch.float32).contiguous()
+    kc = key_cache.to(torch.float32).contiguous()
+    vc = value_cache.to(torch.float32).contiguous()
+    gs = gather_slots.to(torch.int32).contiguous()
+    m = attention_mask.to(torch.uint8).contiguous()
+    dims = N.PagedAttentionDims(q.shape[1], q.shape[2], q.shape[3], kc.shape[0], kc.shape[1],
+                                kc.shape[2], kc.shape[3], gs.shape[0])
+    if dims.num_query_heads % dims.num_kv_heads != 0:
+        raise RuntimeError("num_query_heads must be a multiple of num_kv_heads for GQA")
+    if layer_idx < 0 or layer_idx >= dims.num_layers:
+        raise RuntimeError("layer_idx out of range")
+    out = torch.empty((1, dims.num_query_tokens, dims.num_query_heads, dims.head_dim),
+                      dtype=torch.float32, device=q.device)
+    if dims.num_query_tokens == 0:
+        return out
+    L = N.lib()
+    rc = L.b200_paged_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), int(layer_idx), dims,
+                                gs.data_ptr(), m.data_ptr(), float(scaling), out.data_ptr(),
+                                status_word(q.device).data_ptr(), _stream(q.device))
+    N.check(rc)
+    return out

@@ -1,0 +1,187 @@
+"""GPU parity of the attention kernels against the CPU oracle (which is pinned to the reference's
+own kernel by tests/test_oracle.py).  Tolerances from the north-star contract: fp32 paths within
+1e-5 relative (max |diff| / max |ref|), bf16/f16 paths within 2e-2 absolute of the fp32 oracle
+computed on the same (exactly upcast) values."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import device_batch, max_rel, oracle_ragged
+from golden_util import ragged
+
+pytestmark = pytest.mark.gpu
+
+FP32_REL = 1e-5
+BF16_ABS = 2e-2
+
+
+@pytest.fixture(scope="module")
+def ops(pkg):
+    from llm_serving_b200 import paged_ops
+    return paged_ops
+
+
+def test_reference_signature_config1(golden, ops):
+    """Config 1 through the C symbol `paged_attention` (same contract as the reference's)."""
+    from config1_inputs import config1_inputs
+    b, q, kc, vc, gs, mask = config1_inputs()
+    dev = torch.device("cuda")
+    out = ops.paged_attention_masked(torch.from_numpy(q).to(dev), torch.from_numpy(kc).to(dev),
+                                     torch.from_numpy(vc).to(dev), 0,
+                                     torch.from_numpy(gs).to(dev), torch.from_numpy(mask).to(dev),
+                                     b.scale)
+    ref = golden["config1_out"]
+    assert max_rel(out.cpu().numpy(), ref) <= FP32_REL
+    assert ops.read_status(dev) == 0
+
+
+def test_block_table_decode_fp32_config1(golden, ops):
+    from config1_inputs import config1_inputs
+    b, q, kc, vc, gs, mask = config1_inputs()
+    dev = torch.device("cuda")
+    qd = torch.from_numpy(q[0].transpose(1, 0, 2).copy()).to(dev)  # (S, Hq, D)
+    out = ops.paged_decode(qd, torch.from_numpy(kc).to(dev), torch.from_numpy(vc).to(dev), 0,
+                           torch.from_numpy(b.block_tables()).to(dev),
+                           torch.from_numpy(b.context_lens).to(dev), b.scale,
+                           int(b.context_lens.max()))
+    assert max_rel(out.cpu().numpy(), golden["config1_out"][0]) <= FP32_REL
+
+
+def test_golden_cases_masked_and_ragged(golden, ops):
+    dev = torch.device("cuda")
+    for name in golden["attn_cases"]:
+        p = f"attn_{name}_"
+        q, kc, vc = golden[p + "q"], golden[p + "k_cache"], golden[p + "v_cache"]
+        scale = float(golden[p + "scale"])
+        ref = golden[p + "out"]
+        out = ops.paged_attention_masked(torch.from_numpy(q).to(dev), torch.from_numpy(kc).to(dev),
+                                         torch.from_numpy(vc).to(dev), 1,
+                                         torch.from_numpy(golden[p + "gather_slots"]).to(dev),
+                                         torch.from_numpy(golden[p + "mask"]).to(dev), scale)
+        assert max_rel(out.cpu().numpy(), ref) <= FP32_REL, name
+        tables = ragged(golden, p)
+        bt = np.full((len(tables), max(len(t) for t in tables)), -1, np.int32)
+        for i, t in enumerate(tables):
+            bt[i, :len(t)] = t
+        counts = golden[p + "counts"]
+        ctx = (golden[p + "starts"] + counts).astype(np.int32)
+        cu = np.zeros(len(counts) + 1, np.int64)
+        cu[1:] = np.cumsum(counts)
+        qt = torch.from_numpy(q[0].transpose(1, 0, 2).copy()).to(dev)
+        out2 = ops.paged_prefill(qt, torch.from_numpy(kc).to(dev), torch.from_numpy(vc).to(dev), 1,
+                                 torch.from_numpy(bt).to(dev), torch.from_numpy(cu).to(dev),
+                                 torch.from_numpy(ctx).to(dev), scale, int(counts.max()),
+                                 int(ctx.max()))
+        assert max_rel(out2.cpu().numpy(), ref[0]) <= FP32_REL, name
+
+
+def _decode_case(pkg, oracle, ops, b, dtype, seed=0, split=0, layers=1, layer=0):
+    lib = pkg._native.lib()
+    lib.b200_set_decode_split_tokens(split)
+    try:
+        q, kc, vc, bt, ctx = device_batch(b, dtype, seed, num_layers=layers)
+        out = ops.paged_decode(q, kc, vc, layer, bt, ctx, b.scale, int(b.context_lens.max()))
+        torch.cuda.synchronize()
+        ref = oracle_ragged(oracle, b, q, kc, vc, layer)
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        err = np.abs(got - ref).max()
+        assert err <= BF16_ABS, f"max abs err {err}"
+        assert ops.read_status(q.device) == 0
+        return err
+    finally:
+        lib.b200_set_decode_split_tokens(0)
+
+
+def test_decode_bf16_config2(pkg, oracle, ops):
+    """Config 2 (256 sequences, lognormal contexts, GQA 32/8, D 128, bf16): the new token of each
+    sequence is written by reshape_and_cache, then decode reads it back through the table."""
+    b = pkg.workloads.config2(seed=0)
+    q, kc, vc, bt, ctx = device_batch(b, torch.bfloat16, seed=3)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    newk = torch.randn((b.num_seqs, b.num_kv_heads, b.head_dim), generator=g, device="cuda").to(
+        torch.bfloat16)
+    newv = torch.randn((b.num_seqs, b.num_kv_heads, b.head_dim), generator=g, device="cuda").to(
+        torch.bfloat16)
+    slots = torch.from_numpy(b.slot_mapping()).cuda()
+    ops.reshape_and_cache(newk, newv, kc, vc, slots, 0)
+    out = ops.paged_decode(q, kc, vc, 0, bt, ctx, b.scale, int(b.context_lens.max()))
+    torch.cuda.synchronize()
+    ref = oracle_ragged(oracle, b, q, kc, vc)
+    err = np.abs(out.float().cpu().numpy() - ref).max()
+    assert err <= BF16_ABS, err
+    assert ops.read_status(q.device) == 0
+
+
+@pytest.mark.parametrize("hd,bs,hq,hkv,ctx,split", [
+    (128, 16, 32, 8, [1, 2, 15, 16, 17, 31, 33, 100, 511, 512, 513, 1000], 0),
+    (128, 16, 32, 8, [4096, 3000, 16, 1], 64),       # many splits, last-CTA merge
+    (64, 16, 32, 8, [5, 64, 700, 2049], 128),        # config-4 head dim
+    (128, 32, 16, 2, [1, 31, 32, 33, 900], 0),       # block size 32, GQA 8
+    (128, 8, 8, 8, [1, 7, 8, 9, 250], 0),            # block size 8, MHA
+    (128, 16, 32, 2, [17, 400, 1300], 256),          # GQA 16 -> two head chunks
+    (64, 64, 4, 1, [63, 64, 65, 1000], 0),           # MQA, block size 64
+])
+def test_decode_bf16_edge_cases(pkg, oracle, ops, hd, bs, hq, hkv, ctx, split):
+    b = pkg.workloads.custom(seed=len(ctx), context_lens=ctx, new_token_counts=[1] * len(ctx),
+                             num_query_heads=hq, num_kv_heads=hkv, head_dim=hd, block_size=bs)
+    _decode_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd + bs, split=split)
+
+
+def test_decode_f16_and_layer_offset(pkg, oracle, ops):
+    b = pkg.workloads.custom(seed=2, context_lens=[3, 77, 300], new_token_counts=[1, 1, 1],
+                             num_query_heads=16, num_kv_heads=4, head_dim=128, block_size=16)
+    _decode_case(pkg, oracle, ops, b, torch.float16, seed=5, layers=3, layer=2)
+
+
+def test_decode_small_head_dims_use_cuda_core_path(pkg, oracle, ops):
+    # head_dim 8 / 16 (the reference's unit-test shapes) and block size 4 fall outside the
+    # tensor-core tile rules and run on the CUDA-core kernel
+    for hd, bs in ((8, 4), (16, 4), (32, 1)):
+        b = pkg.workloads.custom(seed=hd, context_lens=[1, 5, 9, 33], new_token_counts=[1] * 4,
+                                 num_query_heads=6, num_kv_heads=2, head_dim=hd, block_size=bs)
+        _decode_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd)
+
+
+def test_decode_strided_query_and_rows(pkg, oracle, ops):
+    """HF hands the query over as a transposed view; the kernels take strides, and query_rows
+    places each sequence's row (mixed batches)."""
+    b = pkg.workloads.custom(seed=4, context_lens=[40, 1, 600, 129], new_token_counts=[1] * 4,
+                             num_query_heads=32, num_kv_heads=8, head_dim=128, block_size=16)
+    q, kc, vc, bt, ctx = device_batch(b, torch.bfloat16, seed=11)
+    qbig = torch.zeros((b.num_seqs * 2, 32, 256), dtype=torch.bfloat16, device="cuda")
+    rows = torch.tensor([6, 0, 3, 5], dtype=torch.int32, device="cuda")
+    qbig[rows.long(), :, :128] = q
+    qv = qbig[:, :, :128]
+    out = torch.full((b.num_seqs * 2, 32, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    ops.paged_decode(qv, kc, vc, 0, bt, ctx, b.scale, int(b.context_lens.max()), out=out,
+                     query_rows=rows)
+    ref = oracle_ragged(oracle, b, q, kc, vc)
+    got = out[rows.long()].float().cpu().numpy()
+    assert np.abs(got - ref).max() <= BF16_ABS
+    untouched = [i for i in range(8) if i not in (6, 0, 3, 5)]
+    assert (out[untouched].float() == 7.0).all()
+
+
+def test_decode_empty_context_writes_zeros(pkg, ops):
+    b = pkg.workloads.custom(seed=1, context_lens=[5, 0, 9], new_token_counts=[1, 0, 1],
+                             num_query_heads=8, num_kv_heads=2, head_dim=128, block_size=16)
+    q, kc, vc, bt, ctx = device_batch(b, torch.bfloat16, seed=1)
+    q = torch.randn((3, 8, 128), device="cuda").to(torch.bfloat16)
+    out = torch.full((3, 8, 128), 3.0, dtype=torch.bfloat16, device="cuda")
+    ops.paged_decode(q, kc, vc, 0, bt, ctx, b.scale, 9, out=out)
+    assert (out[1] == 0).all()
+
+
+def test_prefill_mixed_bf16(pkg, oracle, ops):
+    """A mixed ragged step (prefill chunks on cached prefixes + decodes), bf16."""
+    b = pkg.workloads.custom(seed=6, context_lens=[300, 17, 1, 64, 129, 1000],
+                             new_token_counts=[120, 17, 1, 1, 33, 1], num_query_heads=32,
+                             num_kv_heads=8, head_dim=128, block_size=16)
+    q, kc, vc, bt, ctx = device_batch(b, torch.bfloat16, seed=12)
+    cu = torch.from_numpy(b.cu_seqlens()).cuda()
+    out = ops.paged_prefill(q, kc, vc, 0, bt, cu, ctx, b.scale,
+                            int(b.new_token_counts.max()), int(b.context_lens.max()))
+    ref = oracle_ragged(oracle, b, q, kc, vc)
+    assert np.abs(out.float().cpu().numpy() - ref).max() <= BF16_ABS
