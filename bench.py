@@ -248,8 +248,15 @@ def ours_arm(args):
         step()
     torch.cuda.synchronize(dev)
 
+    # Clocks: nvidia-smi samples every 200 ms, longer than a timed region of a few ms, so the
+    # sampler also covers ~0.6 s of the same step run back to back just before the timed steps.
     sampler = ClockSampler(local)
     sampler.start()
+    t_end = time.perf_counter() + 0.6
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     if world > 1:
