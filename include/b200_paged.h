@@ -171,6 +171,10 @@ size_t b200_paged_prefill_workspace_bytes(const B200PrefillParams* p);
 int b200_paged_prefill(const B200PrefillParams* p, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Nonzero: run b200_paged_prefill on the CUDA-core kernel even where the tcgen05 kernel applies
+ * (for A/B comparison); 0 restores the default. */
+void b200_set_prefill_cuda_cores(int32_t enable);
+
 /* ============================================================================================
  * 3. KV-cache slot write (reshape_and_cache)
  * ==========================================================================================*/

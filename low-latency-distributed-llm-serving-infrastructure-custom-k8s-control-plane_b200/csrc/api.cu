@@ -121,6 +121,7 @@ int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows
 }
 
 int g_split_override = 0;
+bool g_force_cuda_core_prefill = false;
 
 struct DecodePlan {
   bool tensor_cores;
@@ -401,15 +402,63 @@ int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t worksp
 
 // ---- prefill (ragged causal) ----------------------------------------------------------------
 
+struct PrefillPlan {
+  bool tensor_cores;
+  int tq;
+  int64_t max_work;
+  size_t off_work, total;
+};
+
+static PrefillPlan make_prefill_plan(const B200PrefillParams& p) {
+  PrefillPlan pl{};
+  const int G = p.num_query_heads / p.geom.num_kv_heads;
+  const int es = esize_of(p.geom.dtype);
+  pl.tensor_cores = (p.geom.dtype == B200_DTYPE_BF16 || p.geom.dtype == B200_DTYPE_F16) &&
+                    (p.geom.head_dim == 64 || p.geom.head_dim == 128) &&
+                    p.geom.block_size % 16 == 0 && G >= 1 && G <= 16 && 128 % G == 0 &&
+                    reinterpret_cast<uintptr_t>(p.query) % 16 == 0 &&
+                    (p.q_stride_token * es) % 16 == 0 && (p.q_stride_head * es) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(p.key_cache) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(p.value_cache) % 16 == 0 &&
+                    static_cast<int64_t>(p.geom.num_layers) * p.geom.total_blocks *
+                            p.geom.block_size < (int64_t(1) << 31);
+  pl.tq = G > 0 ? 128 / G : 128;
+  pl.max_work = static_cast<int64_t>(p.num_tokens) / (pl.tq > 0 ? pl.tq : 1) + p.num_seqs;
+  pl.off_work = align256(sizeof(b200::PrefillHeader));
+  pl.total = pl.tensor_cores ? pl.off_work + align256(pl.max_work * sizeof(int2)) : 0;
+  return pl;
+}
+
+// Q (or any [token][head][dim] tensor of 2-byte elements) as a 4-D map: 64-element chunk,
+// D/64 chunks, heads, tokens; box = one 128-byte row chunk x tq tokens, 128-byte swizzle.
+static int query_tensor_map(const void* q, int64_t stride_tok, int64_t stride_head, int hq,
+                            int ntok, int head_dim, int dtype, int tq, CUtensorMap* out) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(head_dim / 64),
+                              static_cast<cuuint64_t>(hq), static_cast<cuuint64_t>(ntok)};
+  const cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(stride_head * 2),
+                                 static_cast<cuuint64_t>(stride_tok * 2)};
+  const cuuint32_t box[4] = {64, 1, 1, static_cast<cuuint32_t>(tq)};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == B200_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(out, dt, 4, const_cast<void*>(q), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled (query) failed");
+  return B200_OK;
+}
+
 size_t b200_paged_prefill_workspace_bytes(const B200PrefillParams* p) {
-  (void)p;
-  return 0;
+  if (p == nullptr || p->num_seqs <= 0 || p->geom.num_kv_heads <= 0 ||
+      p->num_query_heads % p->geom.num_kv_heads != 0)
+    return 0;
+  return make_prefill_plan(*p).total;
 }
 
 int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t workspace_bytes,
                        void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
   const B200PrefillParams& p = *pp;
   int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
@@ -417,7 +466,67 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
   if (p.num_seqs < 0 || p.num_tokens < 0)
     return fail(B200_ERR_INVALID_ARGUMENT, "negative sizes");
   if (p.num_seqs == 0 || p.num_tokens == 0) return B200_OK;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int G = p.num_query_heads / p.geom.num_kv_heads;
+  const PrefillPlan pl = make_prefill_plan(p);
+  if (pl.tensor_cores && !g_force_cuda_core_prefill) {
+    if (workspace == nullptr || workspace_bytes < pl.total)
+      return fail(B200_ERR_INVALID_ARGUMENT, "prefill workspace too small");
+    if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+      return fail(B200_ERR_INVALID_ARGUMENT, "prefill workspace must be 256-byte aligned");
+    char* ws = static_cast<char*>(workspace);
+    auto* hdr = reinterpret_cast<b200::PrefillHeader*>(ws);
+    auto* work = reinterpret_cast<int2*>(ws + pl.off_work);
+    CUtensorMap qm, km, vm;
+    rc = query_tensor_map(p.query, p.q_stride_token, p.q_stride_head, p.num_query_heads,
+                          p.num_tokens, p.geom.head_dim, p.geom.dtype, pl.tq, &qm);
+    if (rc != B200_OK) return rc;
+    rc = cache_tensor_map(p.key_cache, p.geom, 16, &km);
+    if (rc != B200_OK) return rc;
+    rc = cache_tensor_map(p.value_cache, p.geom, 16, &vm);
+    if (rc != B200_OK) return rc;
+    b200::PrefillPlanArgs pa{};
+    pa.cu_q = p.cu_seqlens;
+    pa.S = p.num_seqs;
+    pa.tq = pl.tq;
+    pa.hkv = p.geom.num_kv_heads;
+    pa.max_work = static_cast<int32_t>(pl.max_work);
+    pa.status = p.status_word;
+    pa.hdr = hdr;
+    pa.work = work;
+    cudaError_t e = b200::launch_prefill_plan(pa, st);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill plan");
+    b200::PrefillArgs a{};
+    a.layer = p.layer_idx;
+    a.nb = p.geom.total_blocks;
+    a.bs = p.geom.block_size;
+    a.hkv = p.geom.num_kv_heads;
+    a.hq = p.num_query_heads;
+    a.group = G;
+    a.tq = pl.tq;
+    a.bt = p.block_tables;
+    a.bt_stride = p.block_table_stride;
+    a.cu_q = p.cu_seqlens;
+    a.ctx_lens = p.context_lens;
+    a.S = p.num_seqs;
+    a.scale_log2 = p.scale * b200::kLog2e;
+    a.out = p.out;
+    a.o_stok = p.o_stride_token;
+    a.o_shead = p.o_stride_head;
+    a.vec_out = (reinterpret_cast<uintptr_t>(p.out) % 16 == 0 && p.o_stride_token % 8 == 0 &&
+                 p.o_stride_head % 8 == 0)
+                    ? 1
+                    : 0;
+    a.status = p.status_word;
+    a.hdr = hdr;
+    a.work = work;
+    const int64_t max_items = pl.max_work * p.geom.num_kv_heads;
+    e = b200::launch_prefill_tc(p.geom.dtype, p.geom.head_dim, qm, km, vm, a,
+                                static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30)),
+                                num_sms(), st);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill");
+    return B200_OK;
+  }
   b200::RowArgs a{};
   a.mode = b200::kRowBlockTable;
   a.q = p.query;
@@ -442,10 +551,12 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
   a.o_srow = p.o_stride_token;
   a.o_shead = p.o_stride_head;
   a.status = p.status_word;
-  cudaError_t e = b200::launch_row(p.geom.dtype, a, p.num_tokens, static_cast<cudaStream_t>(stream));
+  cudaError_t e = b200::launch_row(p.geom.dtype, a, p.num_tokens, st);
   if (e != cudaSuccess) return cuda_fail(e, "paged_prefill(row)");
   return B200_OK;
 }
+
+void b200_set_prefill_cuda_cores(int32_t enable) { g_force_cuda_core_prefill = enable != 0; }
 
 // ---- reshape_and_cache ------------------------------------------------------------------------
 

@@ -93,6 +93,45 @@ struct RowArgs {
   int32_t* status;
 };
 
+constexpr int kPrefillThreads = 192;
+
+struct PrefillHeader {
+  int32_t total_items;
+  int32_t pad[3];
+};
+
+struct PrefillPlanArgs {
+  const int64_t* cu_q;
+  int32_t S;
+  int32_t tq;
+  int32_t hkv;
+  int32_t max_work;
+  int32_t* status;
+  PrefillHeader* hdr;
+  int2* work;
+};
+
+struct PrefillArgs {
+  int32_t layer, nb, bs, hkv, hq, group, tq;
+  const int32_t* bt;
+  int32_t bt_stride;
+  const int64_t* cu_q;
+  const int32_t* ctx_lens;
+  int32_t S;
+  float scale_log2;
+  void* out;
+  int64_t o_stok, o_shead;
+  int32_t vec_out;
+  int32_t* status;
+  const PrefillHeader* hdr;
+  const int2* work;
+};
+
+cudaError_t launch_prefill_plan(const PrefillPlanArgs& a, cudaStream_t stream);
+cudaError_t launch_prefill_tc(int dtype, int head_dim, const CUtensorMap& qm,
+                              const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
+                              int max_items, int num_sms, cudaStream_t stream);
+
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(int dtype, int head_dim, const CUtensorMap& km, const CUtensorMap& vm,
                              const DecodeArgs& a, int max_items, cudaStream_t stream);

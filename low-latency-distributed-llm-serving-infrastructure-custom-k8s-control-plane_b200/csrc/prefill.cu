@@ -1,0 +1,510 @@
+// K3: ragged causal attention on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
+//
+// One work item = (sequence, tile of TQ = 128/G query tokens, KV head).  The 128 query rows of a
+// tile are the G query heads sharing the KV head x TQ tokens (row = g*TQ + t), so every K/V tile
+// fetched from HBM feeds all G heads.  K/V are read through the block table in 64-token tiles.
+//
+// Warp roles (192 threads):
+//   warp 0      TMA producer: Q tile (4-D map over [token][head][dim]), K/V tiles (3-D map over the
+//               paged cache, one 16-row box per block and 64-column half), 2-stage ring.
+//   warp 1      TMEM owner and MMA issuer (one thread): S = Q.K^T into a double-buffered TMEM S
+//               (M=128, N=64, K=D), O += P.V into TMEM O (M=128, N=D, K=64); tcgen05.commit on
+//               mbarriers.  S(j+1) is issued before PV(j), so the tensor core runs while the
+//               softmax warps work on tile j.
+//   warps 2-5   softmax / correction / epilogue, one query row per thread (TMEM lane = row):
+//               tcgen05.ld of S, causal mask, online softmax in fp32, rescale of O in TMEM when
+//               the row max moves, P (bf16) into 128B-swizzled shared memory, final O / l.
+// Every mbarrier wait is bounded; an expired wait records B200_DEVICE_TIMEOUT and stops the CTA.
+#include <type_traits>
+
+#include "attention.cuh"
+#include "tc05.cuh"
+
+namespace b200 {
+
+namespace {
+
+struct SmemLayout {
+  uint32_t q, kv0, p, bars, total;
+};
+
+template <int D>
+__host__ __device__ constexpr SmemLayout prefill_layout() {
+  constexpr uint32_t SUB = D / 64;
+  constexpr uint32_t Q = SUB * 128 * 128;
+  constexpr uint32_t STAGE = 2 * SUB * 64 * 128;
+  constexpr uint32_t P = 128 * 128;
+  return SmemLayout{0, Q, Q + 2 * STAGE, Q + 2 * STAGE + P, Q + 2 * STAGE + P + 256};
+}
+
+enum : int {
+  kBarQFull = 0,
+  kBarQEmpty,
+  kBarKvFull0,
+  kBarKvFull1,
+  kBarKvEmpty0,
+  kBarKvEmpty1,
+  kBarSFull0,
+  kBarSFull1,
+  kBarPFull,
+  kBarPvDone,
+  kBarOEmpty,
+  kBarFinal,
+  kNumBars
+};
+
+// Bounded wait that also gives up when another role has already aborted the CTA.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, volatile int* abort_flag,
+                                              int32_t* status) {
+  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((i & 1023u) == 1023u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  flag_status(status, B200_DEVICE_TIMEOUT);
+  return false;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry_s = 0;
+  __syncthreads();
+  for (int base = 0; base < a.S; base += 1024) {
+    const int s = base + tid;
+    int32_t n = 0;
+    if (s < a.S) {
+      const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
+      n = count > 0 ? static_cast<int32_t>((count + a.tq - 1) / a.tq) : 0;
+    }
+    int32_t v = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t t = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += t;
+    }
+    if (lane == 31) warp_sums[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += t;
+      }
+      warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const int32_t incl = v + (warp > 0 ? warp_sums[warp - 1] : 0) + carry_s;
+    const int32_t excl = incl - n;
+    if (s < a.S)
+      for (int32_t k = 0; k < n; ++k)
+        if (excl + k < a.max_work) a.work[excl + k] = make_int2(s, k);
+        else flag_status(a.status, B200_DEVICE_BAD_OP);
+    __syncthreads();
+    if (tid == 1023) carry_s = incl;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const int32_t tiles = carry_s < a.max_work ? carry_s : a.max_work;
+    a.hdr->total_items = tiles * a.hkv;
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPrefillThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                      const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, PrefillArgs a) {
+  constexpr int SUB = D / 64;
+  constexpr SmemLayout L = prefill_layout<D>();
+  constexpr uint32_t KT = SUB * 64 * 128;  // bytes of one K (or V) tile
+  constexpr uint32_t STAGE = 2 * KT;
+  constexpr uint32_t QBYTES = SUB * 128 * 128;
+  constexpr uint32_t kTmemCols = 256;
+  constexpr uint32_t kColO = 128;
+  constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr uint32_t idesc_s = tc05::idesc_f16(ab_fmt, 128, 64, 0);
+  constexpr uint32_t idesc_o = tc05::idesc_f16(ab_fmt, 128, D, 1);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_u32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    mbar_init(&bars[kBarQFull], 1);
+    mbar_init(&bars[kBarQEmpty], 1);
+    mbar_init(&bars[kBarKvFull0], 1);
+    mbar_init(&bars[kBarKvFull1], 1);
+    mbar_init(&bars[kBarKvEmpty0], 1);
+    mbar_init(&bars[kBarKvEmpty1], 1);
+    mbar_init(&bars[kBarSFull0], 1);
+    mbar_init(&bars[kBarSFull1], 1);
+    mbar_init(&bars[kBarPFull], 128);
+    mbar_init(&bars[kBarPvDone], 1);
+    mbar_init(&bars[kBarOEmpty], 128);
+    mbar_init(&bars[kBarFinal], 1);
+    *abort_flag = 0;
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tc05::tmem_alloc(tmem_slot, kTmemCols);
+    tc05::tmem_relinquish();
+  }
+  tc05::fence_before_sync();
+  __syncthreads();
+  tc05::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int total = a.hdr->total_items;
+
+  auto decode_item = [&](int item, int& s, int& h, int& q_row0, int& n_q, int& pos0, int& kv_end,
+                         int& ctx) {
+    const int pair = item / a.hkv;
+    h = item - pair * a.hkv;
+    const int2 w = a.work[pair];
+    s = w.x;
+    const int64_t q0 = a.cu_q[s];
+    const int count = static_cast<int>(a.cu_q[s + 1] - q0);
+    ctx = a.ctx_lens[s];
+    const int t_begin = w.y * a.tq;
+    n_q = min(a.tq, count - t_begin);
+    q_row0 = static_cast<int>(q0) + t_begin;
+    pos0 = ctx - count + t_begin;
+    kv_end = pos0 + n_q;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      uint32_t n_items = 0, kv_it = 0, q_issued = 0;
+      for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        int s, h, q_row0, n_q, pos0, kv_end, ctx;
+        decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
+        if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
+        ++q_issued;
+        mbar_arrive_expect_tx(&bars[kBarQFull], QBYTES);
+        for (int g = 0; g < a.group; ++g)
+#pragma unroll
+          for (int sub = 0; sub < SUB; ++sub)
+            tc05::tma_load_4d(smem + L.q + sub * 16384 + g * a.tq * 128, &qmap, &bars[kBarQFull],
+                              0, sub, h * a.group + g, q_row0);
+        const int32_t* bt_row = a.bt + static_cast<int64_t>(s) * a.bt_stride;
+        const int n_kv = (kv_end + 63) / 64;
+        bool ok = true;
+        for (int j = 0; j < n_kv && ok; ++j, ++kv_it) {
+          const int st = kv_it & 1;
+          if (!wait_or_abort(&bars[kBarKvEmpty0 + st], ((kv_it >> 1) & 1u) ^ 1u, abort_flag,
+                             a.status)) {
+            ok = false;
+            break;
+          }
+          uint64_t* full = &bars[kBarKvFull0 + st];
+          mbar_arrive_expect_tx(full, STAGE);
+          uint8_t* kdst = smem + L.kv0 + st * STAGE;
+          uint8_t* vdst = kdst + KT;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int tok = j * 64 + 16 * b;
+            const bool real = tok < kv_end;
+            int32_t blk = bt_row[real ? tok / a.bs : 0];
+            if (blk < 0 || blk >= a.nb) {
+              flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+              blk = 0;
+            }
+            const int32_t row = (a.layer * a.nb + blk) * a.bs + (real ? tok % a.bs : 0);
+#pragma unroll
+            for (int sub = 0; sub < SUB; ++sub) {
+              tma_load_3d(kdst + sub * 8192 + b * 2048, &kmap, full, 0, h * SUB + sub, row);
+              tma_load_3d(vdst + sub * 8192 + b * 2048, &vmap, full, 0, h * SUB + sub, row);
+            }
+          }
+        }
+        if (!ok) break;
+        ++n_items;
+      }
+      // Every fill this thread issued has landed before the CTA retires (each barrier's latest
+      // phase belongs to the last fill issued on it; bounded waits).
+      for (uint32_t f = kv_it > 2 ? kv_it - 2 : 0; f < kv_it; ++f)
+        mbar_wait_bounded(&bars[kBarKvFull0 + (f & 1)], (f >> 1) & 1u);
+      if (q_issued > 0) mbar_wait_bounded(&bars[kBarQFull], (q_issued - 1) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t n_items = 0, kv_it = 0, s_it = 0, p_it = 0;
+      const uint32_t q_base = base + L.q;
+      const uint32_t p_base = base + L.p;
+      auto issue_s = [&](uint32_t sbuf, uint32_t stage) {
+        const uint32_t k_base = base + L.kv0 + stage * STAGE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
+          const uint64_t ad = tc05::smem_desc_sw128(q_base + off, 16, 1024);
+          const uint64_t bd = tc05::smem_desc_sw128(k_base + koff, 16, 1024);
+          tc05::mma_f16(tmem + sbuf * 64, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](uint32_t stage, bool acc) {
+        const uint32_t v_base = base + L.kv0 + stage * STAGE + KT;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc05::smem_desc_sw128(p_base + kk * 32, 16, 1024);
+          const uint64_t bd = tc05::smem_desc_sw128(v_base + kk * 2048, 8192, 1024);
+          tc05::mma_f16(tmem + kColO, ad, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        int s, h, q_row0, n_q, pos0, kv_end, ctx;
+        decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
+        const int n_kv = (kv_end + 63) / 64;
+        if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
+        if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
+        tc05::fence_after_sync();
+        bool ok = wait_or_abort(&bars[kBarKvFull0 + (kv_it & 1)], (kv_it >> 1) & 1u, abort_flag,
+                                a.status);
+        if (!ok) break;
+        tc05::fence_after_sync();
+        issue_s(s_it & 1, kv_it & 1);
+        tc05::commit(&bars[kBarSFull0 + (s_it & 1)]);
+        for (int j = 0; j < n_kv; ++j) {
+          const uint32_t kvj = kv_it + j;
+          if (j + 1 < n_kv) {
+            const uint32_t kvn = kvj + 1;
+            if (!wait_or_abort(&bars[kBarKvFull0 + (kvn & 1)], (kvn >> 1) & 1u, abort_flag,
+                               a.status)) {
+              ok = false;
+              break;
+            }
+            tc05::fence_after_sync();
+            issue_s((s_it + j + 1) & 1, kvn & 1);
+            tc05::commit(&bars[kBarSFull0 + ((s_it + j + 1) & 1)]);
+          } else {
+            tc05::commit(&bars[kBarQEmpty]);  // the last S of this item has been issued
+          }
+          if (!wait_or_abort(&bars[kBarPFull], (p_it + j) & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc05::fence_after_sync();
+          issue_pv(kvj & 1, j > 0);
+          tc05::commit(&bars[kBarPvDone]);
+          tc05::commit(&bars[kBarKvEmpty0 + (kvj & 1)]);
+        }
+        if (!ok) break;
+        kv_it += n_kv;
+        s_it += n_kv;
+        p_it += n_kv;
+        ++n_items;
+      }
+      // all tcgen05 work this thread issued completes before TMEM is released
+      tc05::commit(&bars[kBarFinal]);
+      mbar_wait_bounded(&bars[kBarFinal], 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int g = row / a.tq;
+    const int t = row - g * a.tq;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    uint8_t* pbuf = smem + L.p;
+    uint32_t s_it = 0, pv_it = 0, kv_it = 0;
+    const int sm_tid = tid - 64;  // 0..127
+    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+      int s, h, q_row0, n_q, pos0, kv_end, ctx;
+      decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
+      const int n_kv = (kv_end + 63) / 64;
+      const bool valid = t < n_q;
+      const int pos = valid ? pos0 + t : -1;
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const uint32_t sj = s_it + j;
+        ok = wait_or_abort(&bars[kBarSFull0 + (sj & 1)], (sj >> 1) & 1u, abort_flag, a.status);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc05::fence_after_sync();
+        float x[64];
+        {
+          float v0[32], v1[32];
+          tc05::ld_32x32b_x32(trow + (sj & 1) * 64, v0);
+          tc05::ld_32x32b_x32(trow + (sj & 1) * 64 + 32, v1);
+          tc05::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            x[c] = v0[c];
+            x[32 + c] = v1[c];
+          }
+        }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const int kp = j * 64 + c;
+          x[c] = kp <= pos ? x[c] * a.scale_log2 : -INFINITY;
+          mt = fmaxf(mt, x[c]);
+        }
+        const float mn = fmaxf(m, mt);
+        const float mu = mn == -INFINITY ? 0.f : mn;
+        const float alpha = fast_exp2(m - mu);
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          x[c] = fast_exp2(x[c] - mu);
+          rs += x[c];
+        }
+        l = l * alpha + rs;
+        m = mn;
+        if (j > 0) {
+          // PV(j-1) done: O is stable and the P buffer is free
+          ok = wait_or_abort(&bars[kBarPvDone], (pv_it + j - 1) & 1u, abort_flag, a.status);
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+          tc05::fence_after_sync();
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+            for (int ch = 0; ch < D / 32; ++ch) {
+              float o[32];
+              tc05::ld_32x32b_x32(trow + kColO + ch * 32, o);
+              tc05::wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) o[c] *= alpha;
+              tc05::st_32x32b_x32(trow + kColO + ch * 32, o);
+            }
+            tc05::wait_st();
+          }
+        }
+        if (j == n_kv - 1 && kv_end < j * 64 + 64) {
+          // keys past kv_end are masked for every row; their V rows may hold anything -> zero
+          uint8_t* vst = smem + L.kv0 + ((kv_it + j) & 1) * STAGE + KT;
+          const int r0 = kv_end - j * 64;
+          const int nz = (64 - r0) * SUB * 8;  // 16-byte chunks
+          for (int idx = sm_tid; idx < nz; idx += 128) {
+            const int rr = r0 + idx / (SUB * 8);
+            const int rem = idx % (SUB * 8);
+            *reinterpret_cast<uint4*>(vst + (rem >> 3) * 8192 + rr * 128 + (rem & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        // P row (bf16/f16), 128B-swizzled K-major
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint4 v;
+          v.x = MmaOp<T>::pack(x[c8 * 8 + 0], x[c8 * 8 + 1]);
+          v.y = MmaOp<T>::pack(x[c8 * 8 + 2], x[c8 * 8 + 3]);
+          v.z = MmaOp<T>::pack(x[c8 * 8 + 4], x[c8 * 8 + 5]);
+          v.w = MmaOp<T>::pack(x[c8 * 8 + 6], x[c8 * 8 + 7]);
+          *reinterpret_cast<uint4*>(pbuf + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        tc05::fence_before_sync();
+        tc05::mbar_arrive(&bars[kBarPFull]);
+      }
+      if (!ok) break;
+      // epilogue: O / l
+      ok = wait_or_abort(&bars[kBarPvDone], (pv_it + n_kv - 1) & 1u, abort_flag, a.status);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc05::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = static_cast<T*>(a.out) + static_cast<int64_t>(q_row0 + t) * a.o_stok +
+                static_cast<int64_t>(h * a.group + g) * a.o_shead;
+#pragma unroll
+      for (int ch = 0; ch < D / 32; ++ch) {
+        float o[32];
+        tc05::ld_32x32b_x32(trow + kColO + ch * 32, o);
+        tc05::wait_ld();
+        if (valid) {
+          if (a.vec_out) {
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              uint4 v;
+              v.x = MmaOp<T>::pack(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+              v.y = MmaOp<T>::pack(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+              v.z = MmaOp<T>::pack(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+              v.w = MmaOp<T>::pack(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + ch * 32 + c8 * 8) = v;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) orow[ch * 32 + c] = from_f32<T>(o[c] * inv);
+          }
+        }
+      }
+      tc05::fence_before_sync();
+      tc05::mbar_arrive(&bars[kBarOEmpty]);
+      s_it += n_kv;
+      pv_it += n_kv;
+      kv_it += n_kv;
+    }
+  }
+
+  tc05::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc05::fence_after_sync();
+    tc05::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, int D>
+static cudaError_t launch_prefill_tc_t(const CUtensorMap& qm, const CUtensorMap& km,
+                                       const CUtensorMap& vm, const PrefillArgs& a,
+                                       int max_items, int num_sms, cudaStream_t stream) {
+  constexpr SmemLayout L = prefill_layout<D>();
+  // at least ~116 KB so that one CTA (and one 256-column TMEM allocation) sits on each SM
+  const int smem = static_cast<int>(L.total) + 1024 > 118 * 1024 ? static_cast<int>(L.total) + 1024
+                                                                  : 118 * 1024;
+  static bool configured = false;
+  auto kern = prefill_tc_kernel<T, D>;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  int grid = num_sms;
+  if (max_items < grid) grid = max_items;
+  if (grid < 1) grid = 1;
+  kern<<<grid, kPrefillThreads, smem, stream>>>(qm, km, vm, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_plan(const PrefillPlanArgs& a, cudaStream_t stream) {
+  prefill_plan_kernel<<<1, 1024, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_tc(int dtype, int head_dim, const CUtensorMap& qm,
+                              const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
+                              int max_items, int num_sms, cudaStream_t stream) {
+  if (dtype == B200_DTYPE_BF16) {
+    if (head_dim == 128)
+      return launch_prefill_tc_t<__nv_bfloat16, 128>(qm, km, vm, a, max_items, num_sms, stream);
+    if (head_dim == 64)
+      return launch_prefill_tc_t<__nv_bfloat16, 64>(qm, km, vm, a, max_items, num_sms, stream);
+  } else if (dtype == B200_DTYPE_F16) {
+    if (head_dim == 128)
+      return launch_prefill_tc_t<__half, 128>(qm, km, vm, a, max_items, num_sms, stream);
+    if (head_dim == 64)
+      return launch_prefill_tc_t<__half, 64>(qm, km, vm, a, max_items, num_sms, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace b200

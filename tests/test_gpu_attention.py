@@ -185,3 +185,57 @@ def test_prefill_mixed_bf16(pkg, oracle, ops):
                             int(b.new_token_counts.max()), int(b.context_lens.max()))
     ref = oracle_ragged(oracle, b, q, kc, vc)
     assert np.abs(out.float().cpu().numpy() - ref).max() <= BF16_ABS
+
+
+def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False):
+    lib = pkg._native.lib()
+    lib.b200_set_prefill_cuda_cores(1 if cuda_cores else 0)
+    try:
+        q, kc, vc, bt, ctx = device_batch(b, dtype, seed)
+        cu = torch.from_numpy(b.cu_seqlens()).cuda()
+        out = ops.paged_prefill(q, kc, vc, 0, bt, cu, ctx, b.scale, int(b.new_token_counts.max()),
+                                int(b.context_lens.max()))
+        torch.cuda.synchronize()
+        ref = oracle_ragged(oracle, b, q, kc, vc)
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        err = np.abs(got - ref).max()
+        assert err <= BF16_ABS, f"max abs err {err}"
+        assert ops.read_status(q.device) == 0
+        return got
+    finally:
+        lib.b200_set_prefill_cuda_cores(0)
+
+
+@pytest.mark.parametrize("hd,bs,hq,hkv,ctx,cnt", [
+    (128, 16, 32, 8, [300, 17, 1, 64, 129, 1000], [120, 17, 1, 1, 33, 1]),   # mixed, GQA 4
+    (128, 16, 32, 8, [2125], [2125]),                                       # long fresh prompt
+    (128, 16, 32, 8, [64, 65, 63, 127, 128, 129], [64, 1, 63, 30, 128, 2]), # tile edges
+    (64, 16, 32, 8, [700, 90, 33], [200, 90, 5]),                           # head_dim 64
+    (128, 32, 16, 2, [500, 31, 257], [100, 31, 257]),                       # GQA 8, block 32
+    (128, 16, 8, 8, [300, 129], [150, 129]),                                # MHA (128 tokens/tile)
+    (128, 16, 32, 16, [260, 40], [260, 7]),                                 # GQA 2
+])
+def test_prefill_tcgen05_parity(pkg, oracle, ops, hd, bs, hq, hkv, ctx, cnt):
+    b = pkg.workloads.custom(seed=sum(cnt), context_lens=ctx, new_token_counts=cnt,
+                             num_query_heads=hq, num_kv_heads=hkv, head_dim=hd, block_size=bs)
+    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd + hq)
+
+
+def test_prefill_tcgen05_f16_and_agrees_with_cuda_cores(pkg, oracle, ops):
+    b = pkg.workloads.custom(seed=8, context_lens=[333, 70, 12], new_token_counts=[100, 70, 1],
+                             num_query_heads=32, num_kv_heads=8, head_dim=128, block_size=16)
+    _prefill_case(pkg, oracle, ops, b, torch.float16, seed=2)
+    tc = _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=3)
+    cc = _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=3, cuda_cores=True)
+    assert np.abs(tc - cc).max() <= BF16_ABS
+
+
+def test_prefill_config3_subset(pkg, oracle, ops):
+    """4 of config 3's prefill chunks (on their cached prefixes) packed with 16 of its decodes."""
+    full = pkg.workloads.config3(seed=0)
+    idx = [0, 1, 2, 3] + list(range(16, 32))
+    b = pkg.workloads.custom(seed=3, context_lens=full.context_lens[idx],
+                             new_token_counts=full.new_token_counts[idx], num_query_heads=32,
+                             num_kv_heads=8, head_dim=128, block_size=16)
+    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=4)
