@@ -128,6 +128,18 @@ size_t b200_paged_decode_workspace_bytes(const B200DecodeParams* p);
 int b200_paged_decode(const B200DecodeParams* p, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* No counterpart in the reference.  The same decode as b200_paged_decode, for callers that cannot
+ * allocate device memory at decode time (a server that gave nearly all free HBM to its KV block
+ * pool, a plain C caller with no device allocator, a loop that must not pay for cudaMalloc and its
+ * synchronisation): the scratch comes from a static device array of
+ * B200_DECODE_STATIC_SCRATCH_BYTES that every GPU loading this library holds until exit.  Batches
+ * needing more scratch than that (b200_paged_decode_workspace_bytes) are rejected with
+ * B200_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's device address
+ * (make it before any stream capture).  Calls share the array: each call resets what must start at
+ * zero, and calls that overlap on the GPU race.  Allocates nothing. */
+#define B200_DECODE_STATIC_SCRATCH_BYTES ((size_t)64 << 20)
+int b200_paged_decode_static(const B200DecodeParams* p, void* stream);
+
 /* Split size of the decode plan, in tokens (multiple of 16); 0 restores the built-in heuristic
  * (512 tokens, halved while the batch would give fewer than 4 work items per SM). */
 void b200_set_decode_split_tokens(int32_t tokens);

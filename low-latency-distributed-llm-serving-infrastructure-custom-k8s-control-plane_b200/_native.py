@@ -81,6 +81,7 @@ SIGNATURES = [
                                             c_vp, c_f, c_vp, c_vp, c_vp]),
     ("b200_paged_decode_workspace_bytes", c_sz, [ctypes.POINTER(DecodeParams)]),
     ("b200_paged_decode", ctypes.c_int, [ctypes.POINTER(DecodeParams), c_vp, c_sz, c_vp]),
+    ("b200_paged_decode_static", ctypes.c_int, [ctypes.POINTER(DecodeParams), c_vp]),
     ("b200_set_decode_split_tokens", None, [c_i32]),
     ("b200_paged_prefill_workspace_bytes", c_sz, [ctypes.POINTER(PrefillParams)]),
     ("b200_paged_prefill", ctypes.c_int, [ctypes.POINTER(PrefillParams), c_vp, c_sz, c_vp]),
