@@ -370,6 +370,293 @@ def ours_arm(args):
     return 0
 
 
+def attention_flops(b):
+    """QK^T + PV flops of causal attention for every new token: 4 * Hq * D * (position + 1)."""
+    tot = 0
+    for st, c in zip(b.start_positions.astype(np.int64), b.new_token_counts.astype(np.int64)):
+        # sum over positions st..st+c-1 of (pos + 1)
+        tot += 4 * b.num_query_heads * b.head_dim * (c * st + c * (c + 1) // 2)
+    return int(tot)
+
+
+def config3_arm(args):
+    """Mixed ragged step of BASELINE config 3 (16 prefill chunks on cached prefixes + 240 decodes):
+    reshape_and_cache of all new tokens + ragged causal attention over the batch.  Reports the
+    tensor-pipe fraction of the prefill chunks alone and the mixed step's tokens/s."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200 import paged_ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    full = pkg.workloads.config3(seed=0)
+    npre = 16
+    pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
+                               new_token_counts=full.new_token_counts[:npre], num_query_heads=32,
+                               num_kv_heads=8, head_dim=128, block_size=16)
+
+    def setup(b, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        shape = (1, b.total_blocks, b.block_size, b.num_kv_heads, b.head_dim)
+        kc = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randn((b.num_tokens, b.num_query_heads, b.head_dim), generator=g, device=dev).to(torch.bfloat16)
+        nk = torch.randn((b.num_tokens, b.num_kv_heads, b.head_dim), generator=g, device=dev).to(torch.bfloat16)
+        nv = torch.randn((b.num_tokens, b.num_kv_heads, b.head_dim), generator=g, device=dev).to(torch.bfloat16)
+        return dict(kc=kc, vc=vc, q=q, nk=nk, nv=nv, out=torch.empty_like(q),
+                    slots=torch.from_numpy(b.slot_mapping()).to(dev),
+                    bt=torch.from_numpy(b.block_tables()).to(dev),
+                    cu=torch.from_numpy(b.cu_seqlens()).to(dev),
+                    ctx=torch.from_numpy(b.context_lens.astype(np.int32)).to(dev),
+                    mq=int(b.new_token_counts.max()), mc=int(b.context_lens.max()))
+
+    def attn(b, t):
+        paged_ops.paged_prefill(t["q"], t["kc"], t["vc"], 0, t["bt"], t["cu"], t["ctx"], b.scale,
+                                t["mq"], t["mc"], out=t["out"])
+
+    def time_it(fn, steps, warmup):
+        for _ in range(max(warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    tp = setup(pre, 5)
+    ms_pre = time_it(lambda: attn(pre, tp), args.steps, args.warmup)
+    f_pre = attention_flops(pre)
+    tm = setup(full, 6)
+
+    def mixed():
+        paged_ops.reshape_and_cache(tm["nk"], tm["nv"], tm["kc"], tm["vc"], tm["slots"], 0)
+        attn(full, tm)
+
+    ms_mix = time_it(mixed, args.steps, args.warmup)
+    peak = 1675.3
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    tflops = f_pre / (ms_pre * 1e-3) / 1e12
+    line = {
+        "metric": "config3 mixed ragged step: new tokens/s; prefill attention TFLOP/s",
+        "value": round(full.num_tokens / (ms_mix * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_mix, 4),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config3: 16 prefill chunks U[128,2048] on prior U[0,2048] + 240 "
+                               "decodes, GQA 32/8, D 128, BS 16", "new_tokens": full.num_tokens,
+                   "prefill_tokens": pre.num_tokens},
+        "prefill_only": {"ms": round(ms_pre, 4), "flops": f_pre, "tflops": round(tflops, 2),
+                         "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
+                                      "peak": peak, "unit": "TFLOP/s",
+                                      "frac": round(tflops / peak, 4)}},
+        "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
+        "device_status": paged_ops.read_status(dev),
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return world, rank, dev
+
+
+def engine4_arm(args):
+    """random-init Llama (16 x 2048, 32/8 heads, D 64, FFN 8192, vocab 32000,
+    bf16) under continuous batching (max 256 decoding sequences); seeded requests with Poisson
+    arrivals at 20 req/s, prompts lognormal(median 512) <= 4096 tokens of uniform ids, outputs
+    U[64, 512].  The first `--requests` requests of the 2000-request stream are run (the stream
+    is 100 s of arrivals; the prefix keeps a bench call within minutes).  Value: output tokens/s
+    over the run.  Tensor-parallel when launched with torchrun."""
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200.engine import build_engine
+    from llm_serving_b200.model import CONFIG4, kv_bytes_per_token
+    world, rank, dev = _dist_setup()
+    rng = np.random.default_rng(4)
+    n_all = 2000
+    gaps = rng.exponential(1.0 / args.rate, size=n_all)
+    arrivals = np.cumsum(gaps) - gaps[0]
+    plens = np.clip(np.rint(np.exp(rng.normal(math.log(512), 0.8, size=n_all))), 1, 4096).astype(int)
+    olens = rng.integers(64, 513, size=n_all)
+    prompts = [rng.integers(0, CONFIG4.vocab, size=int(L)).tolist() for L in plens[:args.requests]]
+    nreq = args.requests
+    blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(CONFIG4, world) * 16))
+    eng = build_engine(CONFIG4, total_blocks=blocks, block_size=16, rank=rank, world=world,
+                       device=dev, seed=0, max_batch_size=256, max_num_batched_tokens=16384,
+                       max_model_len=8192)
+    # warm-up: a few requests outside the timed run
+    for i in range(4):
+        eng.add_request(prompts[i][:64], max_tokens=8)
+    while eng.has_unfinished_requests():
+        eng.step()
+    torch.cuda.synchronize(dev)
+    eng.tokens_generated = 0
+    if world > 1:
+        dist.barrier()
+    seqs = []
+    admitted = 0
+    flag = torch.zeros(1, dtype=torch.int64, device=dev)
+    t0 = time.perf_counter()
+    while admitted < nreq or eng.has_unfinished_requests():
+        now = time.perf_counter() - t0
+        n_new = 0
+        if rank == 0:
+            while admitted + n_new < nreq and arrivals[admitted + n_new] <= now:
+                n_new += 1
+            if n_new == 0 and not eng.has_unfinished_requests() and admitted < nreq:
+                time.sleep(max(0.0, arrivals[admitted] - now))
+        if world > 1:
+            flag.fill_(n_new)
+            dist.broadcast(flag, 0)
+            n_new = int(flag.item())
+        for i in range(admitted, admitted + n_new):
+            seqs.append(eng.add_request(prompts[i], max_tokens=int(olens[i]),
+                                        arrival=t0 + arrivals[i]))
+        admitted += n_new
+        if eng.has_unfinished_requests():
+            eng.step()
+    torch.cuda.synchronize(dev)
+    elapsed = time.perf_counter() - t0
+    out_tokens = sum(len(s.output_token_ids) for s in seqs)
+    ttft = [s.first_token_time - s.arrival for s in seqs if s.first_token_time]
+    tpot = [(s.finish_time - s.first_token_time) / max(1, len(s.output_token_ids) - 1)
+            for s in seqs if s.finish_time and s.first_token_time]
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "engine output tokens/s (config 4)", "value": round(out_tokens / elapsed, 1),
+        "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "n/a", "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config4 engine, first {nreq} of 2000 Poisson({args.rate}/s) "
+                               "requests, prompts lognormal(512) <= 4096, outputs U[64,512], "
+                               "max 256 decoding sequences, random-init 16x2048 Llama",
+                   "parallelism": f"tp{world}", "kv_pool_blocks": blocks},
+        "elapsed_s": round(elapsed, 3), "output_tokens": out_tokens, "steps": eng.steps,
+        "preemptions": eng.scheduler.preemption_count,
+        "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 2) if ttft else None,
+        "tpot_ms_p50": round(1e3 * float(np.median(tpot)), 3) if tpot else None,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def engine5_arm(args):
+    """random-init Llama-3-8B shape (32 x 4096, 32/8 heads, D 128, FFN 14336,
+    vocab 128256, bf16), tensor-parallel by KV head over the launched ranks.  Long contexts
+    U[8192, 32768] are placed in the cache (K/V filled with random values, blocks handed out by
+    the device pool from a shuffled free list) so that they occupy 95 % of a pool of `--kv-gb`
+    per GPU; then `--steps` engine decode steps run under the continuous-batching scheduler
+    (preemption/recompute if the pool runs dry).  Value: output tokens/s (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200.engine import build_engine, Sequence, SequenceStatus
+    from llm_serving_b200.model import CONFIG5, kv_bytes_per_token
+    world, rank, dev = _dist_setup()
+    shape = CONFIG5
+    bs = 16
+    blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(shape, world) * bs))
+    rng = np.random.default_rng(5)
+    ctxs = []
+    used = 0
+    while True:
+        c = int(rng.integers(8192, 32769))
+        need = -(-c // bs)
+        if used + need > 0.95 * blocks:
+            break
+        ctxs.append(c)
+        used += need
+    eng = build_engine(shape, total_blocks=blocks, block_size=bs, rank=rank, world=world,
+                       device=dev, seed=0, max_batch_size=max(256, len(ctxs)),
+                       max_num_batched_tokens=40000, max_model_len=32768 + 1024)
+    kv, pool = eng.kv, eng.kv.pool
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    for t in (kv.key_cache, kv.value_cache):
+        t.normal_(generator=g)
+    # shuffled free list: fillers take the whole pool, released in random order
+    fillers = 64
+    per = blocks // fillers
+    base_slot = pool.max_seqs - fillers
+    for f in range(fillers):
+        pool.append_tokens(base_slot + f, per * bs)
+    pool.flush()
+    for f in rng.permutation(fillers):
+        pool.release(base_slot + int(f))
+    pool.flush()
+    seqs = []
+    for c in ctxs:
+        s = eng.add_request([1] * c, max_tokens=args.steps + 8)
+        eng.scheduler.waiting.remove(s)
+        kv.allocate_prefix_blocks(s)
+        s.output_token_ids.append(2)          # as if prefilled: the next step decodes
+        s.status = SequenceStatus.RUNNING
+        eng.scheduler.running.append(s)
+        seqs.append(s)
+    # the cache holds random K/V for every allocated token (no prefill pass: decode is measured)
+    pool.flush()
+    for _ in range(max(args.warmup, 2)):
+        eng.step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gen0 = eng.tokens_generated
+    e0.record()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    toks = eng.tokens_generated - gen0
+    tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    ms = float(tt.item())
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "engine output tokens/s (config 5, decode at long context)",
+        "value": round(toks / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config5: Llama-3-8B shape random init, contexts U[8192,32768] at "
+                               "95% pool occupancy (shuffled free list), decode steps",
+                   "parallelism": f"tp{world} (KV heads)", "sequences": len(ctxs),
+                   "sum_ctx": int(sum(ctxs)), "kv_pool_blocks_per_gpu": blocks,
+                   "kv_gb_per_gpu": args.kv_gb},
+        "preemptions": eng.scheduler.preemption_count, "wall_s": round(wall, 3),
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -380,7 +667,18 @@ def main():
     ap.add_argument("--split", type=int, default=0, help="decode split tokens (0 = heuristic)")
     ap.add_argument("--cpu-seqs", type=int, default=32)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5"],
+                    default="config2")
+    ap.add_argument("--requests", type=int, default=200, help="engine4: requests to run")
+    ap.add_argument("--rate", type=float, default=20.0, help="engine4: arrivals per second")
+    ap.add_argument("--kv-gb", type=float, default=40.0, help="engine: KV pool GB per GPU")
     args = ap.parse_args()
+    if args.workload == "config3":
+        return config3_arm(args)
+    if args.workload == "engine4":
+        return engine4_arm(args)
+    if args.workload == "engine5":
+        return engine5_arm(args)
     if args.impl == "reference":
         return reference_arm(args)
     return ours_arm(args)

@@ -79,6 +79,12 @@ class DeviceBlockPool:
     def get_num_free_blocks(self) -> int:
         return int(N.lib().b200_pool_num_free_blocks(self._h))
 
+    def get_total_blocks(self) -> int:
+        return self.total_blocks
+
+    def get_block_size(self) -> int:
+        return self.block_size
+
     def tokens(self, slot: int) -> int:
         return int(N.lib().b200_pool_tokens(self._h, int(slot)))
 

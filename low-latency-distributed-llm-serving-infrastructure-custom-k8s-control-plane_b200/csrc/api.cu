@@ -282,15 +282,14 @@ size_t b200_paged_decode_workspace_bytes(const B200DecodeParams* p) {
   return make_decode_plan(*p).total;
 }
 
-int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t workspace_bytes,
-                      void* stream) {
-  if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
-  const B200DecodeParams& p = *pp;
-  int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
-  if (rc != B200_OK) return rc;
-  if (p.num_seqs < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_seqs < 0");
-  if (p.num_seqs == 0) return B200_OK;
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+namespace {
+// Decode over block tables.  cu_q != NULL: mixed batch, only sequences with exactly one new
+// token (row cu_q[s]) are attended; the others are left to the prefill kernel.
+int run_decode(const B200DecodeParams& p, const int64_t* cu_q, void* workspace,
+               size_t workspace_bytes, cudaStream_t st) {
+  int rc = B200_OK;
   const int G = p.num_query_heads / p.geom.num_kv_heads;
   const DecodePlan pl = make_decode_plan(p);
   if (!pl.tensor_cores) {
@@ -345,6 +344,7 @@ int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t worksp
   b200::PlanArgs pa{};
   pa.ctx_lens = p.context_lens;
   pa.query_rows = p.query_rows;
+  pa.cu_q = cu_q;
   pa.S = p.num_seqs;
   pa.max_ctx = p.max_context_len;
   pa.split_tokens = pl.split_tokens;
@@ -368,6 +368,7 @@ int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t worksp
   a.q_srow = p.q_stride_row;
   a.q_shead = p.q_stride_head;
   a.query_rows = p.query_rows;
+  a.cu_q = cu_q;
   a.layer = p.layer_idx;
   a.nb = p.geom.total_blocks;
   a.bs = p.geom.block_size;
@@ -399,15 +400,56 @@ int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t worksp
   if (e != cudaSuccess) return cuda_fail(e, "decode");
   return B200_OK;
 }
+}  // namespace
+
+extern "C" {
+
+int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
+  const B200DecodeParams& p = *pp;
+  int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
+  if (rc != B200_OK) return rc;
+  if (p.num_seqs < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_seqs < 0");
+  if (p.num_seqs == 0) return B200_OK;
+  return run_decode(p, nullptr, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
 
 // ---- prefill (ragged causal) ----------------------------------------------------------------
 
 struct PrefillPlan {
   bool tensor_cores;
+  bool split_decodes;  // one-token sequences go to the split-K decode kernel
   int tq;
   int64_t max_work;
-  size_t off_work, total;
+  size_t decode_bytes, off_hdr, off_work, total;
 };
+
+// The decode leg of a mixed batch: every sequence, filtered on the device to those with one
+// new token (their query row is cu_seqlens[s]).
+static B200DecodeParams decode_leg(const B200PrefillParams& p) {
+  B200DecodeParams d{};
+  d.query = p.query;
+  d.q_stride_row = p.q_stride_token;
+  d.q_stride_head = p.q_stride_head;
+  d.query_rows = nullptr;
+  d.key_cache = p.key_cache;
+  d.value_cache = p.value_cache;
+  d.geom = p.geom;
+  d.layer_idx = p.layer_idx;
+  d.num_query_heads = p.num_query_heads;
+  d.block_tables = p.block_tables;
+  d.block_table_stride = p.block_table_stride;
+  d.context_lens = p.context_lens;
+  d.num_seqs = p.num_seqs;
+  d.max_context_len = p.max_context_len;
+  d.scale = p.scale;
+  d.out = p.out;
+  d.o_stride_row = p.o_stride_token;
+  d.o_stride_head = p.o_stride_head;
+  d.status_word = p.status_word;
+  return d;
+}
 
 static PrefillPlan make_prefill_plan(const B200PrefillParams& p) {
   PrefillPlan pl{};
@@ -424,7 +466,11 @@ static PrefillPlan make_prefill_plan(const B200PrefillParams& p) {
                             p.geom.block_size < (int64_t(1) << 31);
   pl.tq = G > 0 ? 128 / G : 128;
   pl.max_work = static_cast<int64_t>(p.num_tokens) / (pl.tq > 0 ? pl.tq : 1) + p.num_seqs;
-  pl.off_work = align256(sizeof(b200::PrefillHeader));
+  const DecodePlan dpl = make_decode_plan(decode_leg(p));
+  pl.split_decodes = pl.tensor_cores && dpl.tensor_cores;
+  pl.decode_bytes = pl.split_decodes ? align256(dpl.total) : 0;
+  pl.off_hdr = pl.decode_bytes;
+  pl.off_work = pl.off_hdr + align256(sizeof(b200::PrefillHeader));
   pl.total = pl.tensor_cores ? pl.off_work + align256(pl.max_work * sizeof(int2)) : 0;
   return pl;
 }
@@ -475,7 +521,11 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
       return fail(B200_ERR_INVALID_ARGUMENT, "prefill workspace must be 256-byte aligned");
     char* ws = static_cast<char*>(workspace);
-    auto* hdr = reinterpret_cast<b200::PrefillHeader*>(ws);
+    if (pl.split_decodes) {
+      rc = run_decode(decode_leg(p), p.cu_seqlens, ws, pl.decode_bytes, st);
+      if (rc != B200_OK) return rc;
+    }
+    auto* hdr = reinterpret_cast<b200::PrefillHeader*>(ws + pl.off_hdr);
     auto* work = reinterpret_cast<int2*>(ws + pl.off_work);
     CUtensorMap qm, km, vm;
     rc = query_tensor_map(p.query, p.q_stride_token, p.q_stride_head, p.num_query_heads,
@@ -487,6 +537,7 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     if (rc != B200_OK) return rc;
     b200::PrefillPlanArgs pa{};
     pa.cu_q = p.cu_seqlens;
+    pa.skip_single = pl.split_decodes ? 1 : 0;
     pa.S = p.num_seqs;
     pa.tq = pl.tq;
     pa.hkv = p.geom.num_kv_heads;

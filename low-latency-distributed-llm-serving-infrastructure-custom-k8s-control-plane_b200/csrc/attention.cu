@@ -32,13 +32,15 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
   for (int base = 0; base < a.S; base += 1024) {
     const int s = base + tid;
     int32_t n = 0;
+    bool decoded = true;
     if (s < a.S) {
       int32_t ctx = a.ctx_lens[s];
       if (ctx > a.max_ctx) {
         flag_status(a.status, B200_DEVICE_BAD_OP);
         ctx = a.max_ctx;
       }
-      n = ctx > 0 ? (ctx + a.split_tokens - 1) / a.split_tokens : 0;
+      if (a.cu_q != nullptr && a.cu_q[s + 1] - a.cu_q[s] != 1) decoded = false;
+      n = (decoded && ctx > 0) ? (ctx + a.split_tokens - 1) / a.split_tokens : 0;
     }
     // block-wide inclusive scan: warp shuffles, then one warp over the warp totals
     int32_t v = n;
@@ -65,8 +67,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     if (s < a.S) {
       a.cu_splits[s] = excl;
       for (int32_t p = 0; p < n; ++p) a.work_sp[excl + p] = make_int2(s, p);
-      if (n == 0) {  // empty context: the reference writes zeros (paged_kernels.cpp:30-34)
-        const int64_t row = a.query_rows ? a.query_rows[s] : s;
+      if (n == 0 && decoded) {  // empty context: the reference writes zeros (paged_kernels.cpp:30-34)
+        const int64_t row = a.cu_q ? a.cu_q[s] : (a.query_rows ? a.query_rows[s] : s);
         char* orow = static_cast<char*>(a.out) + row * a.o_srow * a.esize;
         for (int h = 0; h < a.hq; ++h)
           for (int d = 0; d < a.head_dim; ++d)
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     const int nunits = (tok_end - tok_begin + 15) >> 4;
     const int nh = min(8, a.group - cch * 8);  // q heads of this chunk
     const int hq0 = h * a.group + cch * 8;
-    const int64_t qrow = a.query_rows ? a.query_rows[s] : s;
+    const int64_t qrow = a.cu_q ? a.cu_q[s] : (a.query_rows ? a.query_rows[s] : s);
     const int32_t* bt_row = a.bt + static_cast<int64_t>(s) * a.bt_stride;
     const int n_my = nunits > warp ? (nunits - warp + NW - 1) / NW : 0;
 

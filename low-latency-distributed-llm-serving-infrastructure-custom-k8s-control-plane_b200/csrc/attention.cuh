@@ -28,6 +28,7 @@ struct DecodeHeader {
 struct PlanArgs {
   const int32_t* ctx_lens;
   const int32_t* query_rows;
+  const int64_t* cu_q;  // mixed batch: only sequences with exactly one new token are decoded
   int32_t S;
   int32_t max_ctx;
   int32_t split_tokens;
@@ -48,6 +49,7 @@ struct DecodeArgs {
   const void* q;
   int64_t q_srow, q_shead;
   const int32_t* query_rows;
+  const int64_t* cu_q;  // mixed batch: the query row of sequence s is cu_q[s]
   int32_t layer, nb, bs, hkv, hq, group, nchunks, hpc;
   const int32_t* bt;
   int32_t bt_stride;
@@ -102,6 +104,7 @@ struct PrefillHeader {
 
 struct PrefillPlanArgs {
   const int64_t* cu_q;
+  int32_t skip_single;  // sequences with one new token go to the decode kernel instead
   int32_t S;
   int32_t tq;
   int32_t hkv;

@@ -44,20 +44,25 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase completes (or the
+// hint, in ns, runs out) instead of spinning and taking issue slots from the warps that do the
+// work on the same SM sub-partition.
+constexpr uint32_t kWaitHintNs = 1000000;  // 1 ms per try
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(kWaitHintNs)
       : "memory");
   return ok != 0;
 }
 
-// Each try_wait suspends for a hardware-chosen interval; the bound keeps any wait finite.
-constexpr uint32_t kMaxWaitIters = 1u << 22;
+// At most kMaxWaitIters tries of up to kWaitHintNs each: every wait ends within seconds.
+constexpr uint32_t kMaxWaitIters = 4096;
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
   for (uint32_t i = 0; i < kMaxWaitIters; ++i)

@@ -24,27 +24,32 @@ namespace b200 {
 
 namespace {
 
+// K and V stream through separate rings of kStages tiles: a K stage is released as soon as its
+// S = Q.K^T has completed, a V stage when its PV has, so loads run ahead of both MMAs.
+constexpr int kStages = 3;
+
 struct SmemLayout {
-  uint32_t q, kv0, p, bars, total;
+  uint32_t q, k0, v0, p, bars, total;
 };
 
 template <int D>
 __host__ __device__ constexpr SmemLayout prefill_layout() {
   constexpr uint32_t SUB = D / 64;
   constexpr uint32_t Q = SUB * 128 * 128;
-  constexpr uint32_t STAGE = 2 * SUB * 64 * 128;
+  constexpr uint32_t KT = SUB * 64 * 128;
   constexpr uint32_t P = 128 * 128;
-  return SmemLayout{0, Q, Q + 2 * STAGE, Q + 2 * STAGE + P, Q + 2 * STAGE + P + 256};
+  return SmemLayout{0, Q, Q + kStages * KT, Q + 2 * kStages * KT, Q + 2 * kStages * KT + P,
+                    Q + 2 * kStages * KT + P + 512};
 }
 
 enum : int {
   kBarQFull = 0,
   kBarQEmpty,
-  kBarKvFull0,
-  kBarKvFull1,
-  kBarKvEmpty0,
-  kBarKvEmpty1,
-  kBarSFull0,
+  kBarKFull,                      // + stage
+  kBarKEmpty = kBarKFull + kStages,
+  kBarVFull = kBarKEmpty + kStages,
+  kBarVEmpty = kBarVFull + kStages,
+  kBarSFull0 = kBarVEmpty + kStages,
   kBarSFull1,
   kBarPFull,
   kBarPvDone,
@@ -58,7 +63,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, vol
                                               int32_t* status) {
   for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
-    if ((i & 1023u) == 1023u && *abort_flag) return false;
+    if (*abort_flag) return false;
   }
   *abort_flag = 1;
   flag_status(status, B200_DEVICE_TIMEOUT);
@@ -78,7 +83,9 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
     int32_t n = 0;
     if (s < a.S) {
       const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
-      n = count > 0 ? static_cast<int32_t>((count + a.tq - 1) / a.tq) : 0;
+      n = (count > 0 && !(a.skip_single && count == 1))
+              ? static_cast<int32_t>((count + a.tq - 1) / a.tq)
+              : 0;
     }
     int32_t v = n;
 #pragma unroll
@@ -122,7 +129,6 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   constexpr int SUB = D / 64;
   constexpr SmemLayout L = prefill_layout<D>();
   constexpr uint32_t KT = SUB * 64 * 128;  // bytes of one K (or V) tile
-  constexpr uint32_t STAGE = 2 * KT;
   constexpr uint32_t QBYTES = SUB * 128 * 128;
   constexpr uint32_t kTmemCols = 256;
   constexpr uint32_t kColO = 128;
@@ -142,10 +148,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   if (tid == 0) {
     mbar_init(&bars[kBarQFull], 1);
     mbar_init(&bars[kBarQEmpty], 1);
-    mbar_init(&bars[kBarKvFull0], 1);
-    mbar_init(&bars[kBarKvFull1], 1);
-    mbar_init(&bars[kBarKvEmpty0], 1);
-    mbar_init(&bars[kBarKvEmpty1], 1);
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&bars[kBarKFull + st], 1);
+      mbar_init(&bars[kBarKEmpty + st], 1);
+      mbar_init(&bars[kBarVFull + st], 1);
+      mbar_init(&bars[kBarVEmpty + st], 1);
+    }
     mbar_init(&bars[kBarSFull0], 1);
     mbar_init(&bars[kBarSFull1], 1);
     mbar_init(&bars[kBarPFull], 128);
@@ -203,16 +211,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const int n_kv = (kv_end + 63) / 64;
         bool ok = true;
         for (int j = 0; j < n_kv && ok; ++j, ++kv_it) {
-          const int st = kv_it & 1;
-          if (!wait_or_abort(&bars[kBarKvEmpty0 + st], ((kv_it >> 1) & 1u) ^ 1u, abort_flag,
-                             a.status)) {
-            ok = false;
-            break;
-          }
-          uint64_t* full = &bars[kBarKvFull0 + st];
-          mbar_arrive_expect_tx(full, STAGE);
-          uint8_t* kdst = smem + L.kv0 + st * STAGE;
-          uint8_t* vdst = kdst + KT;
+          const uint32_t st = kv_it % kStages;
+          const uint32_t ph = ((kv_it / kStages) & 1u) ^ 1u;
+          int32_t rows[4];
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const int tok = j * 64 + 16 * b;
@@ -222,21 +223,42 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
               flag_status(a.status, B200_DEVICE_BAD_BLOCK);
               blk = 0;
             }
-            const int32_t row = (a.layer * a.nb + blk) * a.bs + (real ? tok % a.bs : 0);
-#pragma unroll
-            for (int sub = 0; sub < SUB; ++sub) {
-              tma_load_3d(kdst + sub * 8192 + b * 2048, &kmap, full, 0, h * SUB + sub, row);
-              tma_load_3d(vdst + sub * 8192 + b * 2048, &vmap, full, 0, h * SUB + sub, row);
-            }
+            rows[b] = (a.layer * a.nb + blk) * a.bs + (real ? tok % a.bs : 0);
           }
+          if (!wait_or_abort(&bars[kBarKEmpty + st], ph, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars[kBarKFull + st], KT);
+          uint8_t* kdst = smem + L.k0 + st * KT;
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+#pragma unroll
+            for (int sub = 0; sub < SUB; ++sub)
+              tma_load_3d(kdst + sub * 8192 + b * 2048, &kmap, &bars[kBarKFull + st], 0,
+                          h * SUB + sub, rows[b]);
+          if (!wait_or_abort(&bars[kBarVEmpty + st], ph, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars[kBarVFull + st], KT);
+          uint8_t* vdst = smem + L.v0 + st * KT;
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+#pragma unroll
+            for (int sub = 0; sub < SUB; ++sub)
+              tma_load_3d(vdst + sub * 8192 + b * 2048, &vmap, &bars[kBarVFull + st], 0,
+                          h * SUB + sub, rows[b]);
         }
         if (!ok) break;
         ++n_items;
       }
       // Every fill this thread issued has landed before the CTA retires (each barrier's latest
       // phase belongs to the last fill issued on it; bounded waits).
-      for (uint32_t f = kv_it > 2 ? kv_it - 2 : 0; f < kv_it; ++f)
-        mbar_wait_bounded(&bars[kBarKvFull0 + (f & 1)], (f >> 1) & 1u);
+      for (uint32_t f = kv_it > kStages ? kv_it - kStages : 0; f < kv_it; ++f) {
+        mbar_wait_bounded(&bars[kBarKFull + f % kStages], (f / kStages) & 1u);
+        mbar_wait_bounded(&bars[kBarVFull + f % kStages], (f / kStages) & 1u);
+      }
       if (q_issued > 0) mbar_wait_bounded(&bars[kBarQFull], (q_issued - 1) & 1u);
     }
     __syncwarp();
@@ -247,7 +269,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       const uint32_t q_base = base + L.q;
       const uint32_t p_base = base + L.p;
       auto issue_s = [&](uint32_t sbuf, uint32_t stage) {
-        const uint32_t k_base = base + L.kv0 + stage * STAGE;
+        const uint32_t k_base = base + L.k0 + stage * KT;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -258,7 +280,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
       };
       auto issue_pv = [&](uint32_t stage, bool acc) {
-        const uint32_t v_base = base + L.kv0 + stage * STAGE + KT;
+        const uint32_t v_base = base + L.v0 + stage * KT;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint64_t ad = tc05::smem_desc_sw128(p_base + kk * 32, 16, 1024);
@@ -273,35 +295,39 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
         if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
         tc05::fence_after_sync();
-        bool ok = wait_or_abort(&bars[kBarKvFull0 + (kv_it & 1)], (kv_it >> 1) & 1u, abort_flag,
-                                a.status);
+        bool ok = wait_or_abort(&bars[kBarKFull + kv_it % kStages], (kv_it / kStages) & 1u,
+                                abort_flag, a.status);
         if (!ok) break;
         tc05::fence_after_sync();
-        issue_s(s_it & 1, kv_it & 1);
+        issue_s(s_it & 1, kv_it % kStages);
         tc05::commit(&bars[kBarSFull0 + (s_it & 1)]);
+        tc05::commit(&bars[kBarKEmpty + kv_it % kStages]);
         for (int j = 0; j < n_kv; ++j) {
           const uint32_t kvj = kv_it + j;
           if (j + 1 < n_kv) {
             const uint32_t kvn = kvj + 1;
-            if (!wait_or_abort(&bars[kBarKvFull0 + (kvn & 1)], (kvn >> 1) & 1u, abort_flag,
-                               a.status)) {
+            if (!wait_or_abort(&bars[kBarKFull + kvn % kStages], (kvn / kStages) & 1u,
+                               abort_flag, a.status)) {
               ok = false;
               break;
             }
             tc05::fence_after_sync();
-            issue_s((s_it + j + 1) & 1, kvn & 1);
+            issue_s((s_it + j + 1) & 1, kvn % kStages);
             tc05::commit(&bars[kBarSFull0 + ((s_it + j + 1) & 1)]);
+            tc05::commit(&bars[kBarKEmpty + kvn % kStages]);
           } else {
             tc05::commit(&bars[kBarQEmpty]);  // the last S of this item has been issued
           }
-          if (!wait_or_abort(&bars[kBarPFull], (p_it + j) & 1u, abort_flag, a.status)) {
+          if (!wait_or_abort(&bars[kBarPFull], (p_it + j) & 1u, abort_flag, a.status) ||
+              !wait_or_abort(&bars[kBarVFull + kvj % kStages], (kvj / kStages) & 1u, abort_flag,
+                             a.status)) {
             ok = false;
             break;
           }
           tc05::fence_after_sync();
-          issue_pv(kvj & 1, j > 0);
+          issue_pv(kvj % kStages, j > 0);
           tc05::commit(&bars[kBarPvDone]);
-          tc05::commit(&bars[kBarKvEmpty0 + (kvj & 1)]);
+          tc05::commit(&bars[kBarVEmpty + kvj % kStages]);
         }
         if (!ok) break;
         kv_it += n_kv;
@@ -352,24 +378,45 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             x[32 + c] = v1[c];
           }
         }
-        float mt = -INFINITY;
+        // causal mask only where some row of this warp ends inside the tile
+        const bool need_mask = __any_sync(0xffffffffu, j * 64 + 63 > pos);
+        if (need_mask) {
+          const int lim = pos - j * 64;  // columns c > lim are in the future of this row
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c > lim) x[c] = -INFINITY;
+        }
+        // 8 independent partial maxima (one softmax warp per SM sub-partition: keep the
+        // dependent chains short)
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = x[k];
+#pragma unroll
+        for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], x[c]);
+        const float smax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        // Online softmax with a lazily moved reference max: the row keeps using its current
+        // reference m until the tile max exceeds it by more than 8 (log2 units), so p stays below
+        // 2^8 and O / l are rescaled only on such jumps.  O and l always share the same m, so the
+        // final O / l is exact whichever m was used.
+        const float tmax = smax * a.scale_log2;  // scale > 0: max commutes with scaling
+        float alpha = 1.f;
+        if (m == -INFINITY) {
+          m = tmax;                    // first keys of this row (O holds nothing yet)
+        } else if (tmax > m + 8.f) {
+          alpha = fast_exp2(m - tmax);
+          m = tmax;
+        }
+        const float mu = m == -INFINITY ? 0.f : m;
+        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const int kp = j * 64 + c;
-          x[c] = kp <= pos ? x[c] * a.scale_log2 : -INFINITY;
-          mt = fmaxf(mt, x[c]);
+          x[c] = fast_exp2(fmaf(x[c], a.scale_log2, -mu));
+          rs8[c & 7] += x[c];
         }
-        const float mn = fmaxf(m, mt);
-        const float mu = mn == -INFINITY ? 0.f : mn;
-        const float alpha = fast_exp2(m - mu);
-        float rs = 0.f;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          x[c] = fast_exp2(x[c] - mu);
-          rs += x[c];
-        }
+        const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
+                         ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         l = l * alpha + rs;
-        m = mn;
         if (j > 0) {
           // PV(j-1) done: O is stable and the P buffer is free
           ok = wait_or_abort(&bars[kBarPvDone], (pv_it + j - 1) & 1u, abort_flag, a.status);
@@ -393,7 +440,15 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
         if (j == n_kv - 1 && kv_end < j * 64 + 64) {
           // keys past kv_end are masked for every row; their V rows may hold anything -> zero
-          uint8_t* vst = smem + L.kv0 + ((kv_it + j) & 1) * STAGE + KT;
+          // (after the V tile has landed)
+          const uint32_t fv = kv_it + j;
+          ok = wait_or_abort(&bars[kBarVFull + fv % kStages], (fv / kStages) & 1u, abort_flag,
+                             a.status);
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+          uint8_t* vst = smem + L.v0 + (fv % kStages) * KT;
           const int r0 = kv_end - j * 64;
           const int nz = (64 - r0) * SUB * 8;  // 16-byte chunks
           for (int idx = sm_tid; idx < nz; idx += 128) {
