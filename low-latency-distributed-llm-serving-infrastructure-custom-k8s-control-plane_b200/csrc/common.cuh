@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a paged-attention kernels: status flags, mbarrier and TMA
-// wrappers (plain, never multicast), warp-level tensor-core fragments (ldmatrix / mma.sync /
+// wrappers (each load lands in its own CTA only), warp-level tensor-core fragments (ldmatrix / mma.sync /
 // movmatrix) and bf16/f16 packing.
 #pragma once
 
@@ -75,7 +75,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA: 3-D tiled load global -> shared, completion on an mbarrier.  No multicast.
+// TMA: 3-D tiled load global -> shared of this CTA, completion on an mbarrier.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2) {

@@ -27,6 +27,10 @@ namespace {
 // K and V stream through separate rings of kStages tiles: a K stage is released as soon as its
 // S = Q.K^T has completed, a V stage when its PV has, so loads run ahead of both MMAs.
 constexpr int kStages = 3;
+// S = Q.K^T runs up to two tiles ahead of the softmax (three TMEM S buffers); P is
+// double-buffered so the softmax of tile j+1 never waits for PV(j) unless it must rescale O.
+constexpr int kSBufs = 3;
+constexpr int kPBufs = 2;
 
 struct SmemLayout {
   uint32_t q, k0, v0, p, bars, total;
@@ -38,8 +42,8 @@ __host__ __device__ constexpr SmemLayout prefill_layout() {
   constexpr uint32_t Q = SUB * 128 * 128;
   constexpr uint32_t KT = SUB * 64 * 128;
   constexpr uint32_t P = 128 * 128;
-  return SmemLayout{0, Q, Q + kStages * KT, Q + 2 * kStages * KT, Q + 2 * kStages * KT + P,
-                    Q + 2 * kStages * KT + P + 512};
+  return SmemLayout{0, Q, Q + kStages * KT, Q + 2 * kStages * KT,
+                    Q + 2 * kStages * KT + kPBufs * P, Q + 2 * kStages * KT + kPBufs * P + 512};
 }
 
 enum : int {
@@ -49,11 +53,10 @@ enum : int {
   kBarKEmpty = kBarKFull + kStages,
   kBarVFull = kBarKEmpty + kStages,
   kBarVEmpty = kBarVFull + kStages,
-  kBarSFull0 = kBarVEmpty + kStages,
-  kBarSFull1,
-  kBarPFull,
-  kBarPvDone,
-  kBarOEmpty,
+  kBarSFull = kBarVEmpty + kStages,  // + S buffer
+  kBarPFull = kBarSFull + kSBufs,     // + P buffer
+  kBarPvDone = kBarPFull + kPBufs,    // + P buffer
+  kBarOEmpty = kBarPvDone + kPBufs,
   kBarFinal,
   kNumBars
 };
@@ -130,8 +133,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   constexpr SmemLayout L = prefill_layout<D>();
   constexpr uint32_t KT = SUB * 64 * 128;  // bytes of one K (or V) tile
   constexpr uint32_t QBYTES = SUB * 128 * 128;
-  constexpr uint32_t kTmemCols = 256;
-  constexpr uint32_t kColO = 128;
+  constexpr uint32_t kTmemCols = 512;
+  constexpr uint32_t kColO = 256;
   constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t idesc_s = tc05::idesc_f16(ab_fmt, 128, 64, 0);
   constexpr uint32_t idesc_o = tc05::idesc_f16(ab_fmt, 128, D, 1);
@@ -154,11 +157,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       mbar_init(&bars[kBarVFull + st], 1);
       mbar_init(&bars[kBarVEmpty + st], 1);
     }
-    mbar_init(&bars[kBarSFull0], 1);
-    mbar_init(&bars[kBarSFull1], 1);
-    mbar_init(&bars[kBarPFull], 128);
-    mbar_init(&bars[kBarPvDone], 1);
-    mbar_init(&bars[kBarOEmpty], 128);
+    for (int b = 0; b < kSBufs; ++b) mbar_init(&bars[kBarSFull + b], 1);
+    for (int b = 0; b < kPBufs; ++b) {
+      mbar_init(&bars[kBarPFull + b], 4);  // one arrival per softmax warp
+      mbar_init(&bars[kBarPvDone + b], 1);
+    }
+    mbar_init(&bars[kBarOEmpty], 4);
     mbar_init(&bars[kBarFinal], 1);
     *abort_flag = 0;
     fence_proxy_async_smem();
@@ -210,6 +214,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const int32_t* bt_row = a.bt + static_cast<int64_t>(s) * a.bt_stride;
         const int n_kv = (kv_end + 63) / 64;
         bool ok = true;
+        // block ids of the next tile are read one tile ahead, so their global-load latency
+        // overlaps the waits and TMA issue of the current tile
+        int32_t nblk[4];
+        auto fetch_blocks = [&](int jj) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int tok = jj * 64 + 16 * b;
+            nblk[b] = bt_row[tok < kv_end ? tok / a.bs : 0];
+          }
+        };
+        fetch_blocks(0);
         for (int j = 0; j < n_kv && ok; ++j, ++kv_it) {
           const uint32_t st = kv_it % kStages;
           const uint32_t ph = ((kv_it / kStages) & 1u) ^ 1u;
@@ -218,13 +233,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           for (int b = 0; b < 4; ++b) {
             const int tok = j * 64 + 16 * b;
             const bool real = tok < kv_end;
-            int32_t blk = bt_row[real ? tok / a.bs : 0];
+            int32_t blk = nblk[b];
             if (blk < 0 || blk >= a.nb) {
               flag_status(a.status, B200_DEVICE_BAD_BLOCK);
               blk = 0;
             }
             rows[b] = (a.layer * a.nb + blk) * a.bs + (real ? tok % a.bs : 0);
           }
+          if (j + 1 < n_kv) fetch_blocks(j + 1);
           if (!wait_or_abort(&bars[kBarKEmpty + st], ph, abort_flag, a.status)) {
             ok = false;
             break;
@@ -265,7 +281,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t n_items = 0, kv_it = 0, s_it = 0, p_it = 0;
+      uint32_t n_items = 0, kv_it = 0, s_it = 0;
       const uint32_t q_base = base + L.q;
       const uint32_t p_base = base + L.p;
       auto issue_s = [&](uint32_t sbuf, uint32_t stage) {
@@ -279,14 +295,25 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           tc05::mma_f16(tmem + sbuf * 64, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t stage, bool acc) {
+      auto issue_pv = [&](uint32_t stage, uint32_t pbuf, bool acc) {
         const uint32_t v_base = base + L.v0 + stage * KT;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc05::smem_desc_sw128(p_base + kk * 32, 16, 1024);
+          const uint64_t ad =
+              tc05::smem_desc_sw128(p_base + pbuf * 16384 + kk * 32, 16, 1024);
           const uint64_t bd = tc05::smem_desc_sw128(v_base + kk * 2048, 8192, 1024);
           tc05::mma_f16(tmem + kColO, ad, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
         }
+      };
+      auto issue_s_tile = [&](uint32_t g, uint32_t f) -> bool {  // S(g) from K fill f
+        if (!wait_or_abort(&bars[kBarKFull + f % kStages], (f / kStages) & 1u, abort_flag,
+                           a.status))
+          return false;
+        tc05::fence_after_sync();
+        issue_s(g % kSBufs, f % kStages);
+        tc05::commit(&bars[kBarSFull + g % kSBufs]);
+        tc05::commit(&bars[kBarKEmpty + f % kStages]);
+        return true;
       };
       for (int item = blockIdx.x; item < total; item += gridDim.x) {
         int s, h, q_row0, n_q, pos0, kv_end, ctx;
@@ -295,44 +322,36 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
         if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
         tc05::fence_after_sync();
-        bool ok = wait_or_abort(&bars[kBarKFull + kv_it % kStages], (kv_it / kStages) & 1u,
-                                abort_flag, a.status);
+        bool ok = true;
+        // S(0), S(1) ahead; then PV(j) followed by S(j+2)
+        for (int j = 0; j < 2 && j < n_kv && ok; ++j) ok = issue_s_tile(s_it + j, kv_it + j);
         if (!ok) break;
-        tc05::fence_after_sync();
-        issue_s(s_it & 1, kv_it % kStages);
-        tc05::commit(&bars[kBarSFull0 + (s_it & 1)]);
-        tc05::commit(&bars[kBarKEmpty + kv_it % kStages]);
+        if (n_kv <= 2) tc05::commit(&bars[kBarQEmpty]);
         for (int j = 0; j < n_kv; ++j) {
-          const uint32_t kvj = kv_it + j;
-          if (j + 1 < n_kv) {
-            const uint32_t kvn = kvj + 1;
-            if (!wait_or_abort(&bars[kBarKFull + kvn % kStages], (kvn / kStages) & 1u,
-                               abort_flag, a.status)) {
-              ok = false;
-              break;
-            }
-            tc05::fence_after_sync();
-            issue_s((s_it + j + 1) & 1, kvn % kStages);
-            tc05::commit(&bars[kBarSFull0 + ((s_it + j + 1) & 1)]);
-            tc05::commit(&bars[kBarKEmpty + kvn % kStages]);
-          } else {
-            tc05::commit(&bars[kBarQEmpty]);  // the last S of this item has been issued
-          }
-          if (!wait_or_abort(&bars[kBarPFull], (p_it + j) & 1u, abort_flag, a.status) ||
-              !wait_or_abort(&bars[kBarVFull + kvj % kStages], (kvj / kStages) & 1u, abort_flag,
+          const uint32_t g = s_it + j;
+          const uint32_t f = kv_it + j;
+          if (!wait_or_abort(&bars[kBarPFull + g % kPBufs], (g / kPBufs) & 1u, abort_flag,
+                             a.status) ||
+              !wait_or_abort(&bars[kBarVFull + f % kStages], (f / kStages) & 1u, abort_flag,
                              a.status)) {
             ok = false;
             break;
           }
           tc05::fence_after_sync();
-          issue_pv(kvj % kStages, j > 0);
-          tc05::commit(&bars[kBarPvDone]);
-          tc05::commit(&bars[kBarVEmpty + kvj % kStages]);
+          issue_pv(f % kStages, g % kPBufs, j > 0);
+          tc05::commit(&bars[kBarPvDone + g % kPBufs]);
+          tc05::commit(&bars[kBarVEmpty + f % kStages]);
+          if (j + 2 < n_kv) {
+            if (!issue_s_tile(g + 2, f + 2)) {
+              ok = false;
+              break;
+            }
+            if (j + 2 == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);  // last S of the item
+          }
         }
         if (!ok) break;
         kv_it += n_kv;
         s_it += n_kv;
-        p_it += n_kv;
         ++n_items;
       }
       // all tcgen05 work this thread issued completes before TMEM is released
@@ -347,8 +366,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const int g = row / a.tq;
     const int t = row - g * a.tq;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    uint8_t* pbuf = smem + L.p;
-    uint32_t s_it = 0, pv_it = 0, kv_it = 0;
+    uint32_t s_it = 0, kv_it = 0;
     const int sm_tid = tid - 64;  // 0..127
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
       int s, h, q_row0, n_q, pos0, kv_end, ctx;
@@ -359,8 +377,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
-        const uint32_t sj = s_it + j;
-        ok = wait_or_abort(&bars[kBarSFull0 + (sj & 1)], (sj >> 1) & 1u, abort_flag, a.status);
+        const uint32_t gt = s_it + j;  // tile number across items (barrier phases)
+        ok = wait_or_abort(&bars[kBarSFull + gt % kSBufs], (gt / kSBufs) & 1u, abort_flag,
+                           a.status);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
           break;
@@ -369,8 +388,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         float x[64];
         {
           float v0[32], v1[32];
-          tc05::ld_32x32b_x32(trow + (sj & 1) * 64, v0);
-          tc05::ld_32x32b_x32(trow + (sj & 1) * 64 + 32, v1);
+          tc05::ld_32x32b_x32(trow + (gt % kSBufs) * 64, v0);
+          tc05::ld_32x32b_x32(trow + (gt % kSBufs) * 64 + 32, v1);
           tc05::wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
@@ -417,15 +436,27 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
                          ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         l = l * alpha + rs;
-        if (j > 0) {
-          // PV(j-1) done: O is stable and the P buffer is free
-          ok = wait_or_abort(&bars[kBarPvDone], (pv_it + j - 1) & 1u, abort_flag, a.status);
+        if (gt >= kPBufs) {
+          // this P buffer was last read by PV(gt - 2): wait until that MMA has completed
+          const uint32_t pg = gt - kPBufs;
+          ok = wait_or_abort(&bars[kBarPvDone + pg % kPBufs], (pg / kPBufs) & 1u, abort_flag,
+                             a.status);
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+        }
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          // rescaling O needs PV(gt - 1) to have landed in TMEM
+          const uint32_t pg = gt - 1;
+          ok = wait_or_abort(&bars[kBarPvDone + pg % kPBufs], (pg / kPBufs) & 1u, abort_flag,
+                             a.status);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
           }
           tc05::fence_after_sync();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          {
 #pragma unroll
             for (int ch = 0; ch < D / 32; ++ch) {
               float o[32];
@@ -459,6 +490,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           }
         }
         // P row (bf16/f16), 128B-swizzled K-major
+        uint8_t* pbuf = smem + L.p + (gt % kPBufs) * 16384;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           uint4 v;
@@ -470,11 +502,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
         fence_proxy_async_smem();
         tc05::fence_before_sync();
-        tc05::mbar_arrive(&bars[kBarPFull]);
+        __syncwarp();
+        if (lane == 0) tc05::mbar_arrive(&bars[kBarPFull + gt % kPBufs]);
       }
       if (!ok) break;
-      // epilogue: O / l
-      ok = wait_or_abort(&bars[kBarPvDone], (pv_it + n_kv - 1) & 1u, abort_flag, a.status);
+      // epilogue: O / l after the item's last PV
+      const uint32_t gl = s_it + n_kv - 1;
+      ok = wait_or_abort(&bars[kBarPvDone + gl % kPBufs], (gl / kPBufs) & 1u, abort_flag,
+                         a.status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc05::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -503,9 +538,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
       }
       tc05::fence_before_sync();
-      tc05::mbar_arrive(&bars[kBarOEmpty]);
+      __syncwarp();
+      if (lane == 0) tc05::mbar_arrive(&bars[kBarOEmpty]);
       s_it += n_kv;
-      pv_it += n_kv;
       kv_it += n_kv;
     }
   }
