@@ -95,7 +95,7 @@ struct RowArgs {
   int32_t* status;
 };
 
-constexpr int kPrefillThreads = 192;
+constexpr int kPrefillThreads = 224;
 
 struct PrefillHeader {
   int32_t total_items;

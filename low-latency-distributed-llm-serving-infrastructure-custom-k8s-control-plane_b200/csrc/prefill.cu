@@ -4,13 +4,16 @@
 // tile are the G query heads sharing the KV head x TQ tokens (row = g*TQ + t), so every K/V tile
 // fetched from HBM feeds all G heads.  K/V are read through the block table in 64-token tiles.
 //
-// Warp roles (192 threads):
-//   warp 0      TMA producer: Q tile (4-D map over [token][head][dim]), K/V tiles (3-D map over the
-//               paged cache, one 16-row box per block and 64-column half), 2-stage ring.
-//   warp 1      TMEM owner and MMA issuer (one thread): S = Q.K^T into a double-buffered TMEM S
+// Warp roles (224 threads):
+//   warp 0      TMA producer for Q (4-D map over [token][head][dim]) and K tiles (3-D map over the
+//               paged cache, one 16-row box per block and 64-column half), kKStages-deep ring.
+//   warp 6      TMA producer for V tiles, kVStages-deep ring.  K and V are issued by different
+//               threads: a block-paged tile is 4*D/64 small boxes, and one thread issuing both
+//               rings could not keep the tensor core fed.
+//   warp 1      TMEM owner and MMA issuer (one thread): S = Q.K^T into a triple-buffered TMEM S
 //               (M=128, N=64, K=D), O += P.V into TMEM O (M=128, N=D, K=64); tcgen05.commit on
-//               mbarriers.  S(j+1) is issued before PV(j), so the tensor core runs while the
-//               softmax warps work on tile j.
+//               mbarriers.  S(j+2) is issued right after PV(j), so the tensor core runs while the
+//               softmax warps work on tile j+1.
 //   warps 2-5   softmax / correction / epilogue, one query row per thread (TMEM lane = row):
 //               tcgen05.ld of S, causal mask, online softmax in fp32, rescale of O in TMEM when
 //               the row max moves, P (bf16) into 128B-swizzled shared memory, final O / l.
@@ -24,9 +27,11 @@ namespace b200 {
 
 namespace {
 
-// K and V stream through separate rings of kStages tiles: a K stage is released as soon as its
-// S = Q.K^T has completed, a V stage when its PV has, so loads run ahead of both MMAs.
-constexpr int kStages = 3;
+// K and V stream through separate rings: a K stage is released as soon as its S = Q.K^T has
+// completed, a V stage when its PV has, so loads run ahead of both MMAs.  K is needed one tile
+// earlier than V (S(j+2) is issued before PV(j+1)), hence the deeper K ring.
+constexpr int kKStages = 4;
+constexpr int kVStages = 3;
 // S = Q.K^T runs up to two tiles ahead of the softmax (three TMEM S buffers); P is
 // double-buffered so the softmax of tile j+1 never waits for PV(j) unless it must rescale O.
 constexpr int kSBufs = 3;
@@ -42,18 +47,18 @@ __host__ __device__ constexpr SmemLayout prefill_layout() {
   constexpr uint32_t Q = SUB * 128 * 128;
   constexpr uint32_t KT = SUB * 64 * 128;
   constexpr uint32_t P = 128 * 128;
-  return SmemLayout{0, Q, Q + kStages * KT, Q + 2 * kStages * KT,
-                    Q + 2 * kStages * KT + kPBufs * P, Q + 2 * kStages * KT + kPBufs * P + 512};
+  constexpr uint32_t KV = (kKStages + kVStages) * KT;
+  return SmemLayout{0, Q, Q + kKStages * KT, Q + KV, Q + KV + kPBufs * P, Q + KV + kPBufs * P + 512};
 }
 
 enum : int {
   kBarQFull = 0,
   kBarQEmpty,
-  kBarKFull,                      // + stage
-  kBarKEmpty = kBarKFull + kStages,
-  kBarVFull = kBarKEmpty + kStages,
-  kBarVEmpty = kBarVFull + kStages,
-  kBarSFull = kBarVEmpty + kStages,  // + S buffer
+  kBarKFull,                          // + K stage
+  kBarKEmpty = kBarKFull + kKStages,
+  kBarVFull = kBarKEmpty + kKStages,  // + V stage
+  kBarVEmpty = kBarVFull + kVStages,
+  kBarSFull = kBarVEmpty + kVStages,  // + S buffer
   kBarPFull = kBarSFull + kSBufs,     // + P buffer
   kBarPvDone = kBarPFull + kPBufs,    // + P buffer
   kBarOEmpty = kBarPvDone + kPBufs,
@@ -151,9 +156,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   if (tid == 0) {
     mbar_init(&bars[kBarQFull], 1);
     mbar_init(&bars[kBarQEmpty], 1);
-    for (int st = 0; st < kStages; ++st) {
+    for (int st = 0; st < kKStages; ++st) {
       mbar_init(&bars[kBarKFull + st], 1);
       mbar_init(&bars[kBarKEmpty + st], 1);
+    }
+    for (int st = 0; st < kVStages; ++st) {
       mbar_init(&bars[kBarVFull + st], 1);
       mbar_init(&bars[kBarVEmpty + st], 1);
     }
@@ -193,88 +200,86 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     kv_end = pos0 + n_q;
   };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------------------------ TMA producers
     if (lane == 0) {
-      prefetch_tensormap(&qmap);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
+      const bool is_k = warp == 0;
+      const CUtensorMap* map = is_k ? &kmap : &vmap;
+      const uint32_t nst = is_k ? kKStages : kVStages;
+      uint64_t* full = &bars[is_k ? kBarKFull : kBarVFull];
+      uint64_t* empty = &bars[is_k ? kBarKEmpty : kBarVEmpty];
+      uint8_t* ring = smem + (is_k ? L.k0 : L.v0);
+      if (is_k) prefetch_tensormap(&qmap);
+      prefetch_tensormap(map);
+      const int32_t layer_base = a.layer * a.nb;
       uint32_t n_items = 0, kv_it = 0, q_issued = 0;
       for (int item = blockIdx.x; item < total; item += gridDim.x) {
         int s, h, q_row0, n_q, pos0, kv_end, ctx;
         decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
-        if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
-        ++q_issued;
-        mbar_arrive_expect_tx(&bars[kBarQFull], QBYTES);
-        for (int g = 0; g < a.group; ++g)
+        if (is_k) {
+          if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
+          ++q_issued;
+          mbar_arrive_expect_tx(&bars[kBarQFull], QBYTES);
+          for (int g = 0; g < a.group; ++g)
 #pragma unroll
-          for (int sub = 0; sub < SUB; ++sub)
-            tc05::tma_load_4d(smem + L.q + sub * 16384 + g * a.tq * 128, &qmap, &bars[kBarQFull],
-                              0, sub, h * a.group + g, q_row0);
+            for (int sub = 0; sub < SUB; ++sub)
+              tc05::tma_load_4d(smem + L.q + sub * 16384 + g * a.tq * 128, &qmap,
+                                &bars[kBarQFull], 0, sub, h * a.group + g, q_row0);
+        }
         const int32_t* bt_row = a.bt + static_cast<int64_t>(s) * a.bt_stride;
         const int n_kv = (kv_end + 63) / 64;
         bool ok = true;
-        // block ids of the next tile are read one tile ahead, so their global-load latency
-        // overlaps the waits and TMA issue of the current tile
-        int32_t nblk[4];
-        auto fetch_blocks = [&](int jj) {
+        // Cache rows of the next tile's four 16-row chunks, read one tile ahead so the
+        // block-table load latency overlaps the current tile's wait and TMA issue.  (fb, fw) =
+        // block index and row within the block of the next chunk; chunks past kv_end load
+        // (masked) rows of the sequence's first block.
+        int fb = 0, fw = 0;
+        int32_t nrow[4];
+        auto fetch_rows = [&](int jj) {
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
-            const int tok = jj * 64 + 16 * b;
-            nblk[b] = bt_row[tok < kv_end ? tok / a.bs : 0];
-          }
-        };
-        fetch_blocks(0);
-        for (int j = 0; j < n_kv && ok; ++j, ++kv_it) {
-          const uint32_t st = kv_it % kStages;
-          const uint32_t ph = ((kv_it / kStages) & 1u) ^ 1u;
-          int32_t rows[4];
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const int tok = j * 64 + 16 * b;
-            const bool real = tok < kv_end;
-            int32_t blk = nblk[b];
+            const bool real = jj * 64 + 16 * b < kv_end;
+            int32_t blk = bt_row[real ? fb : 0];
             if (blk < 0 || blk >= a.nb) {
               flag_status(a.status, B200_DEVICE_BAD_BLOCK);
               blk = 0;
             }
-            rows[b] = (a.layer * a.nb + blk) * a.bs + (real ? tok % a.bs : 0);
+            nrow[b] = (layer_base + blk) * a.bs + (real ? fw : 0);
+            fw += 16;
+            if (fw == a.bs) {
+              fw = 0;
+              ++fb;
+            }
           }
-          if (j + 1 < n_kv) fetch_blocks(j + 1);
-          if (!wait_or_abort(&bars[kBarKEmpty + st], ph, abort_flag, a.status)) {
+        };
+        fetch_rows(0);
+        for (int j = 0; j < n_kv; ++j, ++kv_it) {
+          const uint32_t st = kv_it % nst;
+          const uint32_t ph = ((kv_it / nst) & 1u) ^ 1u;
+          int32_t rows[4];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) rows[b] = nrow[b];
+          if (j + 1 < n_kv) fetch_rows(j + 1);
+          if (!wait_or_abort(&empty[st], ph, abort_flag, a.status)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&bars[kBarKFull + st], KT);
-          uint8_t* kdst = smem + L.k0 + st * KT;
+          mbar_arrive_expect_tx(&full[st], KT);
+          uint8_t* dst = ring + st * KT;
 #pragma unroll
           for (int b = 0; b < 4; ++b)
 #pragma unroll
             for (int sub = 0; sub < SUB; ++sub)
-              tma_load_3d(kdst + sub * 8192 + b * 2048, &kmap, &bars[kBarKFull + st], 0,
-                          h * SUB + sub, rows[b]);
-          if (!wait_or_abort(&bars[kBarVEmpty + st], ph, abort_flag, a.status)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&bars[kBarVFull + st], KT);
-          uint8_t* vdst = smem + L.v0 + st * KT;
-#pragma unroll
-          for (int b = 0; b < 4; ++b)
-#pragma unroll
-            for (int sub = 0; sub < SUB; ++sub)
-              tma_load_3d(vdst + sub * 8192 + b * 2048, &vmap, &bars[kBarVFull + st], 0,
-                          h * SUB + sub, rows[b]);
+              tma_load_3d(dst + sub * 8192 + b * 2048, map, &full[st], 0, h * SUB + sub,
+                          rows[b]);
         }
         if (!ok) break;
         ++n_items;
       }
       // Every fill this thread issued has landed before the CTA retires (each barrier's latest
       // phase belongs to the last fill issued on it; bounded waits).
-      for (uint32_t f = kv_it > kStages ? kv_it - kStages : 0; f < kv_it; ++f) {
-        mbar_wait_bounded(&bars[kBarKFull + f % kStages], (f / kStages) & 1u);
-        mbar_wait_bounded(&bars[kBarVFull + f % kStages], (f / kStages) & 1u);
-      }
+      for (uint32_t f = kv_it > nst ? kv_it - nst : 0; f < kv_it; ++f)
+        mbar_wait_bounded(&full[f % nst], (f / nst) & 1u);
       if (q_issued > 0) mbar_wait_bounded(&bars[kBarQFull], (q_issued - 1) & 1u);
     }
     __syncwarp();
@@ -306,13 +311,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
       };
       auto issue_s_tile = [&](uint32_t g, uint32_t f) -> bool {  // S(g) from K fill f
-        if (!wait_or_abort(&bars[kBarKFull + f % kStages], (f / kStages) & 1u, abort_flag,
+        if (!wait_or_abort(&bars[kBarKFull + f % kKStages], (f / kKStages) & 1u, abort_flag,
                            a.status))
           return false;
         tc05::fence_after_sync();
-        issue_s(g % kSBufs, f % kStages);
+        issue_s(g % kSBufs, f % kKStages);
         tc05::commit(&bars[kBarSFull + g % kSBufs]);
-        tc05::commit(&bars[kBarKEmpty + f % kStages]);
+        tc05::commit(&bars[kBarKEmpty + f % kKStages]);
         return true;
       };
       for (int item = blockIdx.x; item < total; item += gridDim.x) {
@@ -332,15 +337,15 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           const uint32_t f = kv_it + j;
           if (!wait_or_abort(&bars[kBarPFull + g % kPBufs], (g / kPBufs) & 1u, abort_flag,
                              a.status) ||
-              !wait_or_abort(&bars[kBarVFull + f % kStages], (f / kStages) & 1u, abort_flag,
+              !wait_or_abort(&bars[kBarVFull + f % kVStages], (f / kVStages) & 1u, abort_flag,
                              a.status)) {
             ok = false;
             break;
           }
           tc05::fence_after_sync();
-          issue_pv(f % kStages, g % kPBufs, j > 0);
+          issue_pv(f % kVStages, g % kPBufs, j > 0);
           tc05::commit(&bars[kBarPvDone + g % kPBufs]);
-          tc05::commit(&bars[kBarVEmpty + f % kStages]);
+          tc05::commit(&bars[kBarVEmpty + f % kVStages]);
           if (j + 2 < n_kv) {
             if (!issue_s_tile(g + 2, f + 2)) {
               ok = false;
@@ -361,6 +366,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
+    // (warps 2-5: TMEM lane quarter = warp % 4)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int g = row / a.tq;
@@ -473,13 +479,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           // keys past kv_end are masked for every row; their V rows may hold anything -> zero
           // (after the V tile has landed)
           const uint32_t fv = kv_it + j;
-          ok = wait_or_abort(&bars[kBarVFull + fv % kStages], (fv / kStages) & 1u, abort_flag,
+          ok = wait_or_abort(&bars[kBarVFull + fv % kVStages], (fv / kVStages) & 1u, abort_flag,
                              a.status);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
           }
-          uint8_t* vst = smem + L.v0 + (fv % kStages) * KT;
+          uint8_t* vst = smem + L.v0 + (fv % kVStages) * KT;
           const int r0 = kv_end - j * 64;
           const int nz = (64 - r0) * SUB * 8;  // 16-byte chunks
           for (int idx = sm_tid; idx < nz; idx += 128) {
