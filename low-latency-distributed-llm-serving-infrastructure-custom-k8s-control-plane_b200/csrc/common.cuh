@@ -44,30 +44,41 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// try_wait with a suspend-time hint: a waiting thread sleeps until the phase completes (or the
-// hint, in ns, runs out) instead of spinning and taking issue slots from the warps that do the
-// work on the same SM sub-partition.
-constexpr uint32_t kWaitHintNs = 1000000;  // 1 ms per try
-
+// mbarrier.try_wait without a suspend-time hint: the hardware may park the thread for a short,
+// system-dependent time before returning false.  (A large explicit hint made every wait -- even on
+// an already completed phase -- noticeably slower on the single-thread MMA and TMA roles.)
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase), "r"(kWaitHintNs)
+      : "r"(smem_u32(bar)), "r"(phase)
       : "memory");
   return ok != 0;
 }
 
-// At most kMaxWaitIters tries of up to kWaitHintNs each: every wait ends within seconds.
-constexpr uint32_t kMaxWaitIters = 4096;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Every wait is bounded in time: after kWaitLimitNs without the phase completing it gives up
+// (the caller records B200_DEVICE_TIMEOUT and winds the CTA down).  The clock is read once per
+// kWaitTriesPerCheck tries, so a wait that succeeds at once costs a single try_wait.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kWaitTriesPerCheck = 64;
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
-  for (uint32_t i = 0; i < kMaxWaitIters; ++i)
-    if (mbar_try_wait(bar, phase)) return true;
-  return false;
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (uint32_t i = 0; i < kWaitTriesPerCheck; ++i)
+      if (mbar_try_wait(bar, phase)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -4,19 +4,24 @@
 // tile are the G query heads sharing the KV head x TQ tokens (row = g*TQ + t), so every K/V tile
 // fetched from HBM feeds all G heads.  K/V are read through the block table in 64-token tiles.
 //
-// Warp roles (224 threads):
+// Warp roles (352 threads):
 //   warp 0      TMA producer for Q (4-D map over [token][head][dim]) and K tiles (3-D map over the
 //               paged cache, one 16-row box per block and 64-column half), kKStages-deep ring.
-//   warp 6      TMA producer for V tiles, kVStages-deep ring.  K and V are issued by different
+//   warp 10     TMA producer for V tiles, kVStages-deep ring.  K and V are issued by different
 //               threads: a block-paged tile is 4*D/64 small boxes, and one thread issuing both
 //               rings could not keep the tensor core fed.
-//   warp 1      TMEM owner and MMA issuer (one thread): S = Q.K^T into a triple-buffered TMEM S
-//               (M=128, N=64, K=D), O += P.V into TMEM O (M=128, N=D, K=64); tcgen05.commit on
-//               mbarriers.  S(j+2) is issued right after PV(j), so the tensor core runs while the
-//               softmax warps work on tile j+1.
-//   warps 2-5   softmax / correction / epilogue, one query row per thread (TMEM lane = row):
-//               tcgen05.ld of S, causal mask, online softmax in fp32, rescale of O in TMEM when
-//               the row max moves, P (bf16) into 128B-swizzled shared memory, final O / l.
+//   warp 1      TMEM owner and MMA issuer (one thread): S = Q.K^T into four TMEM S slots
+//               (M=128, N=64, K=D), O += P.V (M=128, N=D, K=64) into the accumulator of the
+//               warpgroup that owns the tile; tcgen05.commit on mbarriers.  S(j+4) is issued
+//               right after PV(j), so the tensor core runs ahead of the softmax.
+//   warps 2-5,  two softmax warpgroups.  Warpgroup w takes the KV tiles g with g % 2 == w and keeps
+//   warps 6-9   its own running max / sum and its own O accumulator in TMEM, so the two run
+//               concurrently without exchanging anything per tile (two softmax warps per SM
+//               sub-partition hide each other's ex2 / TMEM latency).  One query row per thread
+//               (TMEM lane = row): tcgen05.ld of S, causal mask, online softmax in fp32, rescale
+//               of O in TMEM when the row max moves, P (bf16/f16) into 128B-swizzled shared memory.
+//               The epilogue merges the two partial (O, max, sum) triples of each row, as a
+//               two-way split-KV combine, and writes O / l.
 // Every mbarrier wait is bounded; an expired wait records B200_DEVICE_TIMEOUT and stops the CTA.
 #include <type_traits>
 
@@ -30,15 +35,16 @@ namespace {
 // K and V stream through separate rings: a K stage is released as soon as its S = Q.K^T has
 // completed, a V stage when its PV has, so loads run ahead of both MMAs.  K is needed one tile
 // earlier than V (S(j+2) is issued before PV(j+1)), hence the deeper K ring.
-constexpr int kKStages = 4;
+constexpr int kKStages = 5;
 constexpr int kVStages = 3;
-// S = Q.K^T runs up to two tiles ahead of the softmax (three TMEM S buffers); P is
-// double-buffered so the softmax of tile j+1 never waits for PV(j) unless it must rescale O.
-constexpr int kSBufs = 3;
+// S = Q.K^T runs up to four tiles ahead of PV (four TMEM S slots, two per softmax warpgroup);
+// one P buffer per softmax warpgroup.
+constexpr int kSBufs = 4;
 constexpr int kPBufs = 2;
+constexpr int kSoftmaxWarps = 8;
 
 struct SmemLayout {
-  uint32_t q, k0, v0, p, bars, total;
+  uint32_t q, k0, v0, p, bars, xch, total;
 };
 
 template <int D>
@@ -48,7 +54,16 @@ __host__ __device__ constexpr SmemLayout prefill_layout() {
   constexpr uint32_t KT = SUB * 64 * 128;
   constexpr uint32_t P = 128 * 128;
   constexpr uint32_t KV = (kKStages + kVStages) * KT;
-  return SmemLayout{0, Q, Q + kKStages * KT, Q + KV, Q + KV + kPBufs * P, Q + KV + kPBufs * P + 512};
+  // xch: per item parity, softmax warpgroup and row, the (max, sum) pair the epilogue merge
+  // exchanges (double-buffered: a warpgroup with no tile in the next item reaches the next
+  // exchange while the other may still read this one)
+  return SmemLayout{0,
+                    Q,
+                    Q + kKStages * KT,
+                    Q + KV,
+                    Q + KV + kPBufs * P,
+                    Q + KV + kPBufs * P + 512,
+                    Q + KV + kPBufs * P + 512 + 2 * 2 * 128 * 8};
 }
 
 enum : int {
@@ -62,16 +77,23 @@ enum : int {
   kBarPFull = kBarSFull + kSBufs,     // + P buffer
   kBarPvDone = kBarPFull + kPBufs,    // + P buffer
   kBarOEmpty = kBarPvDone + kPBufs,
+  kBarXchg,
   kBarFinal,
   kNumBars
 };
 
-// Bounded wait that also gives up when another role has already aborted the CTA.
+// Bounded wait (same time limit as mbar_wait_bounded) that also gives up when another role has
+// already aborted the CTA.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, volatile int* abort_flag,
                                               int32_t* status) {
-  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
-    if (mbar_try_wait(bar, phase)) return true;
-    if (*abort_flag) return false;
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (uint32_t i = 0; i < kWaitTriesPerCheck; ++i) {
+      if (mbar_try_wait(bar, phase)) return true;
+      if (*abort_flag) return false;
+    }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   *abort_flag = 1;
   flag_status(status, B200_DEVICE_TIMEOUT);
@@ -166,10 +188,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     }
     for (int b = 0; b < kSBufs; ++b) mbar_init(&bars[kBarSFull + b], 1);
     for (int b = 0; b < kPBufs; ++b) {
-      mbar_init(&bars[kBarPFull + b], 4);  // one arrival per softmax warp
+      mbar_init(&bars[kBarPFull + b], 4);  // one arrival per warp of the owning warpgroup
       mbar_init(&bars[kBarPvDone + b], 1);
     }
-    mbar_init(&bars[kBarOEmpty], 4);
+    mbar_init(&bars[kBarOEmpty], kSoftmaxWarps);
+    mbar_init(&bars[kBarXchg], kSoftmaxWarps);
     mbar_init(&bars[kBarFinal], 1);
     *abort_flag = 0;
     fence_proxy_async_smem();
@@ -200,7 +223,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     kv_end = pos0 + n_q;
   };
 
-  if (warp == 0 || warp == 6) {
+  if (warp == 0 || warp == 10) {
     // ------------------------------------------------------------------ TMA producers
     if (lane == 0) {
       const bool is_k = warp == 0;
@@ -287,28 +310,33 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t n_items = 0, kv_it = 0, s_it = 0;
-      const uint32_t q_base = base + L.q;
-      const uint32_t p_base = base + L.p;
-      auto issue_s = [&](uint32_t sbuf, uint32_t stage) {
-        const uint32_t k_base = base + L.k0 + stage * KT;
+      // descriptor words built once; every MMA below adds a compile-time K-step offset and a
+      // ring-stage offset to the low word
+      constexpr uint32_t kHi = tc05::desc_hi_sw128(1024);
+      const uint32_t q_lo = tc05::desc_lo(base + L.q, 16);
+      const uint32_t k_lo0 = tc05::desc_lo(base + L.k0, 16);
+      const uint32_t v_lo0 = tc05::desc_lo(base + L.v0, 8192);
+      const uint32_t p_lo0 = tc05::desc_lo(base + L.p, 16);
+      auto issue_s = [&](uint32_t slot, uint32_t stage) {
+        const uint32_t k_lo = k_lo0 + stage * (KT >> 4);
+        const uint32_t d = tmem + slot * 64;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
-          const uint64_t ad = tc05::smem_desc_sw128(q_base + off, 16, 1024);
-          const uint64_t bd = tc05::smem_desc_sw128(k_base + koff, 16, 1024);
-          tc05::mma_f16(tmem + sbuf * 64, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+          const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+          tc05::mma_f16(d, tc05::desc_join(q_lo + qo, kHi), tc05::desc_join(k_lo + ko, kHi),
+                        idesc_s, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t stage, uint32_t pbuf, bool acc) {
-        const uint32_t v_base = base + L.v0 + stage * KT;
+      auto issue_pv = [&](uint32_t stage, uint32_t wg, bool acc) {
+        const uint32_t v_lo = v_lo0 + stage * (KT >> 4);
+        const uint32_t p_lo = p_lo0 + wg * (16384 >> 4);
+        const uint32_t d = tmem + kColO + wg * D;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad =
-              tc05::smem_desc_sw128(p_base + pbuf * 16384 + kk * 32, 16, 1024);
-          const uint64_t bd = tc05::smem_desc_sw128(v_base + kk * 2048, 8192, 1024);
-          tc05::mma_f16(tmem + kColO, ad, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 4; ++kk)
+          tc05::mma_f16(d, tc05::desc_join(p_lo + kk * 2, kHi),
+                        tc05::desc_join(v_lo + kk * (2048 >> 4), kHi), idesc_o,
+                        (acc || kk > 0) ? 1u : 0u);
       };
       auto issue_s_tile = [&](uint32_t g, uint32_t f) -> bool {  // S(g) from K fill f
         if (!wait_or_abort(&bars[kBarKFull + f % kKStages], (f / kKStages) & 1u, abort_flag,
@@ -325,33 +353,36 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
         const int n_kv = (kv_end + 63) / 64;
         if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
-        if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
         tc05::fence_after_sync();
         bool ok = true;
-        // S(0), S(1) ahead; then PV(j) followed by S(j+2)
-        for (int j = 0; j < 2 && j < n_kv && ok; ++j) ok = issue_s_tile(s_it + j, kv_it + j);
+        // the first S tiles of this item overlap the previous item's epilogue (S slots are free:
+        // every P of the previous item has been observed)
+        for (int j = 0; j < kSBufs && j < n_kv && ok; ++j) ok = issue_s_tile(s_it + j, kv_it + j);
         if (!ok) break;
-        if (n_kv <= 2) tc05::commit(&bars[kBarQEmpty]);
+        if (n_kv <= kSBufs) tc05::commit(&bars[kBarQEmpty]);
+        // both O accumulators are free once all softmax warps have read the previous item's O
+        if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
+        tc05::fence_after_sync();
         for (int j = 0; j < n_kv; ++j) {
           const uint32_t g = s_it + j;
           const uint32_t f = kv_it + j;
-          if (!wait_or_abort(&bars[kBarPFull + g % kPBufs], (g / kPBufs) & 1u, abort_flag,
-                             a.status) ||
+          const uint32_t wg = g & 1u;
+          if (!wait_or_abort(&bars[kBarPFull + wg], (g >> 1) & 1u, abort_flag, a.status) ||
               !wait_or_abort(&bars[kBarVFull + f % kVStages], (f / kVStages) & 1u, abort_flag,
                              a.status)) {
             ok = false;
             break;
           }
           tc05::fence_after_sync();
-          issue_pv(f % kVStages, g % kPBufs, j > 0);
-          tc05::commit(&bars[kBarPvDone + g % kPBufs]);
+          issue_pv(f % kVStages, wg, j >= 2);  // tile j-2 went to the same accumulator
+          tc05::commit(&bars[kBarPvDone + wg]);
           tc05::commit(&bars[kBarVEmpty + f % kVStages]);
-          if (j + 2 < n_kv) {
-            if (!issue_s_tile(g + 2, f + 2)) {
+          if (j + kSBufs < n_kv) {
+            if (!issue_s_tile(g + kSBufs, f + kSBufs)) {
               ok = false;
               break;
             }
-            if (j + 2 == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);  // last S of the item
+            if (j + kSBufs == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);  // last S of the item
           }
         }
         if (!ok) break;
@@ -366,24 +397,30 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
-    // (warps 2-5: TMEM lane quarter = warp % 4)
+    // warps 2-5 = warpgroup 0, warps 6-9 = warpgroup 1; TMEM lane quarter = warp % 4
+    const uint32_t wg = static_cast<uint32_t>(warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int g = row / a.tq;
     const int t = row - g * a.tq;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    uint32_t s_it = 0, kv_it = 0;
-    const int sm_tid = tid - 64;  // 0..127
+    const uint32_t o_self = trow + kColO + wg * D;
+    const int sm_tid = (warp - 2 - 4 * static_cast<int>(wg)) * 32 + lane;  // 0..127
+    float2* xch = reinterpret_cast<float2*>(smem + L.xch);
+    uint32_t s_it = 0, kv_it = 0, n_items = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
       int s, h, q_row0, n_q, pos0, kv_end, ctx;
       decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
       const int n_kv = (kv_end + 63) / 64;
       const bool valid = t < n_q;
       const int pos = valid ? pos0 + t : -1;
+      // tiles of this warpgroup: j = j0, j0 + 2, ... (global tile number g = s_it + j, g % 2 == wg)
+      const int j0 = static_cast<int>((s_it ^ wg) & 1u);
       float m = -INFINITY, l = 0.f;
       bool ok = true;
-      for (int j = 0; j < n_kv; ++j) {
-        const uint32_t gt = s_it + j;  // tile number across items (barrier phases)
+      int j = j0;
+      for (; j < n_kv; j += 2) {
+        const uint32_t gt = s_it + j;
         ok = wait_or_abort(&bars[kBarSFull + gt % kSBufs], (gt / kSBufs) & 1u, abort_flag,
                            a.status);
         if (!__all_sync(0xffffffffu, ok)) {
@@ -411,8 +448,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           for (int c = 0; c < 64; ++c)
             if (c > lim) x[c] = -INFINITY;
         }
-        // 8 independent partial maxima (one softmax warp per SM sub-partition: keep the
-        // dependent chains short)
+        // 8 independent partial maxima keep the dependent chains short
         float mx8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx8[k] = x[k];
@@ -427,7 +463,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const float tmax = smax * a.scale_log2;  // scale > 0: max commutes with scaling
         float alpha = 1.f;
         if (m == -INFINITY) {
-          m = tmax;                    // first keys of this row (O holds nothing yet)
+          m = tmax;                    // first keys of this row in this warpgroup
         } else if (tmax > m + 8.f) {
           alpha = fast_exp2(m - tmax);
           m = tmax;
@@ -442,38 +478,28 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
                          ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         l = l * alpha + rs;
-        if (gt >= kPBufs) {
-          // this P buffer was last read by PV(gt - 2): wait until that MMA has completed
-          const uint32_t pg = gt - kPBufs;
-          ok = wait_or_abort(&bars[kBarPvDone + pg % kPBufs], (pg / kPBufs) & 1u, abort_flag,
-                             a.status);
+        if (gt >= 2) {
+          // this warpgroup's P buffer was last read by PV(gt - 2), which also is the last MMA
+          // into this warpgroup's O: after it completes, P may be overwritten and O rescaled
+          const uint32_t pg = gt - 2;
+          ok = wait_or_abort(&bars[kBarPvDone + wg], (pg >> 1) & 1u, abort_flag, a.status);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
           }
         }
-        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          // rescaling O needs PV(gt - 1) to have landed in TMEM
-          const uint32_t pg = gt - 1;
-          ok = wait_or_abort(&bars[kBarPvDone + pg % kPBufs], (pg / kPBufs) & 1u, abort_flag,
-                             a.status);
-          if (!__all_sync(0xffffffffu, ok)) {
-            ok = false;
-            break;
-          }
+        if (j >= 2 && __any_sync(0xffffffffu, alpha != 1.f)) {
           tc05::fence_after_sync();
-          {
 #pragma unroll
-            for (int ch = 0; ch < D / 32; ++ch) {
-              float o[32];
-              tc05::ld_32x32b_x32(trow + kColO + ch * 32, o);
-              tc05::wait_ld();
+          for (int ch = 0; ch < D / 16; ++ch) {
+            float o[16];
+            tc05::ld_32x32b_x16(o_self + ch * 16, o);
+            tc05::wait_ld();
 #pragma unroll
-              for (int c = 0; c < 32; ++c) o[c] *= alpha;
-              tc05::st_32x32b_x32(trow + kColO + ch * 32, o);
-            }
-            tc05::wait_st();
+            for (int c = 0; c < 16; ++c) o[c] *= alpha;
+            tc05::st_32x32b_x16(o_self + ch * 16, o);
           }
+          tc05::wait_st();
         }
         if (j == n_kv - 1 && kv_end < j * 64 + 64) {
           // keys past kv_end are masked for every row; their V rows may hold anything -> zero
@@ -496,7 +522,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           }
         }
         // P row (bf16/f16), 128B-swizzled K-major
-        uint8_t* pbuf = smem + L.p + (gt % kPBufs) * 16384;
+        uint8_t* pbuf = smem + L.p + wg * 16384;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           uint4 v;
@@ -509,37 +535,74 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         fence_proxy_async_smem();
         tc05::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc05::mbar_arrive(&bars[kBarPFull + gt % kPBufs]);
+        if (lane == 0) tc05::mbar_arrive(&bars[kBarPFull + wg]);
       }
       if (!ok) break;
-      // epilogue: O / l after the item's last PV
-      const uint32_t gl = s_it + n_kv - 1;
-      ok = wait_or_abort(&bars[kBarPvDone + gl % kPBufs], (gl / kPBufs) & 1u, abort_flag,
-                         a.status);
+      // ---- epilogue: wait for this warpgroup's last PV, exchange (m, l) with the other
+      // warpgroup, merge the two partial accumulators (each warpgroup writes half the columns)
+      const bool had_tiles = j0 < n_kv;
+      if (had_tiles) {
+        const uint32_t gl = s_it + static_cast<uint32_t>(j - 2);  // last tile of this warpgroup
+        ok = wait_or_abort(&bars[kBarPvDone + wg], (gl >> 1) & 1u, abort_flag, a.status);
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
+      float2* xb = xch + (n_items & 1u) * 256;
+      xb[wg * 128 + row] = make_float2(m, l);
+      tc05::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc05::mbar_arrive(&bars[kBarXchg]);
+      ok = wait_or_abort(&bars[kBarXchg], n_items & 1u, abort_flag, a.status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc05::fence_after_sync();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float2 other = xb[(wg ^ 1u) * 128 + row];
+      // row max / sum of warpgroup 0 and 1
+      const float m0 = wg == 0 ? m : other.x, l0 = wg == 0 ? l : other.y;
+      const float m1 = wg == 0 ? other.x : m, l1 = wg == 0 ? other.y : l;
+      const float mm = fmaxf(m0, m1);
+      const float f0 = (l0 > 0.f) ? fast_exp2(m0 - mm) : 0.f;
+      const float f1 = (l1 > 0.f) ? fast_exp2(m1 - mm) : 0.f;
+      const float lt = l0 * f0 + l1 * f1;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const float w0 = f0 * inv, w1 = f1 * inv;
+      // an accumulator that received no PV in this item holds stale data: not read at all
+      const bool has0 = static_cast<int>((s_it & 1u)) < n_kv;           // warpgroup 0 had tiles
+      const bool has1 = static_cast<int>(((s_it ^ 1u) & 1u)) < n_kv;    // warpgroup 1 had tiles
       T* orow = static_cast<T*>(a.out) + static_cast<int64_t>(q_row0 + t) * a.o_stok +
                 static_cast<int64_t>(h * a.group + g) * a.o_shead;
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {
-        float o[32];
-        tc05::ld_32x32b_x32(trow + kColO + ch * 32, o);
-        tc05::wait_ld();
+      for (int hc = 0; hc < D / 32; ++hc) {
+        const int c0 = static_cast<int>(wg) * (D / 2) + hc * 16;  // 16-column chunk of O
+        float o[16];
+        if (has0) {
+          tc05::ld_32x32b_x16(trow + kColO + c0, o);
+          tc05::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) o[c] *= w0;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) o[c] = 0.f;
+        }
+        if (has1) {
+          float o1[16];
+          tc05::ld_32x32b_x16(trow + kColO + D + c0, o1);
+          tc05::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) o[c] = fmaf(o1[c], w1, o[c]);
+        }
         if (valid) {
           if (a.vec_out) {
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
+            for (int c8 = 0; c8 < 2; ++c8) {
               uint4 v;
-              v.x = MmaOp<T>::pack(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
-              v.y = MmaOp<T>::pack(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
-              v.z = MmaOp<T>::pack(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
-              v.w = MmaOp<T>::pack(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
-              *reinterpret_cast<uint4*>(orow + ch * 32 + c8 * 8) = v;
+              v.x = MmaOp<T>::pack(o[c8 * 8 + 0], o[c8 * 8 + 1]);
+              v.y = MmaOp<T>::pack(o[c8 * 8 + 2], o[c8 * 8 + 3]);
+              v.z = MmaOp<T>::pack(o[c8 * 8 + 4], o[c8 * 8 + 5]);
+              v.w = MmaOp<T>::pack(o[c8 * 8 + 6], o[c8 * 8 + 7]);
+              *reinterpret_cast<uint4*>(orow + c0 + c8 * 8) = v;
             }
           } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) orow[ch * 32 + c] = from_f32<T>(o[c] * inv);
+            for (int c = 0; c < 16; ++c) orow[c0 + c] = from_f32<T>(o[c]);
           }
         }
       }
@@ -548,6 +611,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       if (lane == 0) tc05::mbar_arrive(&bars[kBarOEmpty]);
       s_it += n_kv;
       kv_it += n_kv;
+      ++n_items;
     }
   }
 
