@@ -2,26 +2,27 @@
 //
 // One work item = (sequence, tile of TQ = 128/G query tokens, KV head).  The 128 query rows of a
 // tile are the G query heads sharing the KV head x TQ tokens (row = g*TQ + t), so every K/V tile
-// fetched from HBM feeds all G heads.  K/V are read through the block table in 64-token tiles.
+// fetched from HBM feeds all G heads.  K/V are read through the block table in 128-key tiles.
 //
 // Warp roles (352 threads):
 //   warp 0      TMA producer for Q (4-D map over [token][head][dim]) and K tiles (3-D map over the
 //               paged cache, one 16-row box per block and 64-column half), kKStages-deep ring.
 //   warp 10     TMA producer for V tiles, kVStages-deep ring.  K and V are issued by different
-//               threads: a block-paged tile is 4*D/64 small boxes, and one thread issuing both
+//               threads: a block-paged tile is 8*D/64 small boxes, and one thread issuing both
 //               rings could not keep the tensor core fed.
-//   warp 1      TMEM owner and MMA issuer (one thread): S = Q.K^T into four TMEM S slots
-//               (M=128, N=64, K=D), O += P.V (M=128, N=D, K=64) into the accumulator of the
-//               warpgroup that owns the tile; tcgen05.commit on mbarriers.  S(j+4) is issued
-//               right after PV(j), so the tensor core runs ahead of the softmax.
+//   warp 1      TMEM owner and MMA issuer (one thread).  S = Q.K^T (M=128, N=128, K=D) into the
+//               TMEM S buffer of the warpgroup that owns the tile; O += P.V (M=128, N=D, K=128)
+//               with P read straight from TMEM (the A operand of tcgen05.mma in tensor memory)
+//               into that warpgroup's O accumulator; tcgen05.commit on mbarriers.
 //   warps 2-5,  two softmax warpgroups.  Warpgroup w takes the KV tiles g with g % 2 == w and keeps
-//   warps 6-9   its own running max / sum and its own O accumulator in TMEM, so the two run
-//               concurrently without exchanging anything per tile (two softmax warps per SM
-//               sub-partition hide each other's ex2 / TMEM latency).  One query row per thread
-//               (TMEM lane = row): tcgen05.ld of S, causal mask, online softmax in fp32, rescale
-//               of O in TMEM when the row max moves, P (bf16/f16) into 128B-swizzled shared memory.
-//               The epilogue merges the two partial (O, max, sum) triples of each row, as a
-//               two-way split-KV combine, and writes O / l.
+//   warps 6-9   its own running max / sum and its own O accumulator, so the two run concurrently
+//               without exchanging anything per tile.  One query row per thread (TMEM lane = row):
+//               tcgen05.ld of S, causal mask, online softmax in fp32, P packed to bf16/f16 pairs
+//               and stored with tcgen05.st over the S columns already consumed, rescale of O in
+//               TMEM when the row max moves.  The epilogue merges the two partial (O, max, sum)
+//               triples of each row, as a two-way split-KV combine, and writes O / l.
+// TMEM (512 columns): S/P of warpgroup w at columns [128w, 128w+128), O of warpgroup w at
+// [256 + w*D, 256 + (w+1)*D).  P(g) aliases S(g), so S(g+2) is issued only after PV(g) completed.
 // Every mbarrier wait is bounded; an expired wait records B200_DEVICE_TIMEOUT and stops the CTA.
 #include <type_traits>
 
@@ -32,38 +33,27 @@ namespace b200 {
 
 namespace {
 
+constexpr int kBN = 128;  // keys per KV tile (the N of S = Q.K^T, the K of O += P.V)
 // K and V stream through separate rings: a K stage is released as soon as its S = Q.K^T has
-// completed, a V stage when its PV has, so loads run ahead of both MMAs.  K is needed one tile
-// earlier than V (S(j+2) is issued before PV(j+1)), hence the deeper K ring.
-constexpr int kKStages = 5;
-constexpr int kVStages = 3;
-// S = Q.K^T runs up to four tiles ahead of PV (four TMEM S slots, two per softmax warpgroup);
-// one P buffer per softmax warpgroup.
-constexpr int kSBufs = 4;
-constexpr int kPBufs = 2;
+// completed, a V stage when its PV has.  K is needed before V, hence the deeper K ring.
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kSoftmaxWarps = 8;
 
 struct SmemLayout {
-  uint32_t q, k0, v0, p, bars, xch, total;
+  uint32_t q, k0, v0, bars, xch, total;
 };
 
 template <int D>
 __host__ __device__ constexpr SmemLayout prefill_layout() {
   constexpr uint32_t SUB = D / 64;
   constexpr uint32_t Q = SUB * 128 * 128;
-  constexpr uint32_t KT = SUB * 64 * 128;
-  constexpr uint32_t P = 128 * 128;
+  constexpr uint32_t KT = SUB * kBN * 128;
   constexpr uint32_t KV = (kKStages + kVStages) * KT;
   // xch: per item parity, softmax warpgroup and row, the (max, sum) pair the epilogue merge
   // exchanges (double-buffered: a warpgroup with no tile in the next item reaches the next
   // exchange while the other may still read this one)
-  return SmemLayout{0,
-                    Q,
-                    Q + kKStages * KT,
-                    Q + KV,
-                    Q + KV + kPBufs * P,
-                    Q + KV + kPBufs * P + 512,
-                    Q + KV + kPBufs * P + 512 + 2 * 2 * 128 * 8};
+  return SmemLayout{0, Q, Q + kKStages * KT, Q + KV, Q + KV + 512, Q + KV + 512 + 2 * 2 * 128 * 8};
 }
 
 enum : int {
@@ -73,10 +63,10 @@ enum : int {
   kBarKEmpty = kBarKFull + kKStages,
   kBarVFull = kBarKEmpty + kKStages,  // + V stage
   kBarVEmpty = kBarVFull + kVStages,
-  kBarSFull = kBarVEmpty + kVStages,  // + S buffer
-  kBarPFull = kBarSFull + kSBufs,     // + P buffer
-  kBarPvDone = kBarPFull + kPBufs,    // + P buffer
-  kBarOEmpty = kBarPvDone + kPBufs,
+  kBarSFull = kBarVEmpty + kVStages,  // + warpgroup
+  kBarPFull = kBarSFull + 2,          // + warpgroup
+  kBarPvDone = kBarPFull + 2,         // + warpgroup
+  kBarOEmpty = kBarPvDone + 2,
   kBarXchg,
   kBarFinal,
   kNumBars
@@ -157,13 +147,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                       const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, PrefillArgs a) {
   constexpr int SUB = D / 64;
+  constexpr int kChunks = kBN / 16;  // 16-row TMA boxes per tile and 64-column half
   constexpr SmemLayout L = prefill_layout<D>();
-  constexpr uint32_t KT = SUB * 64 * 128;  // bytes of one K (or V) tile
+  constexpr uint32_t KT = SUB * kBN * 128;  // bytes of one K (or V) tile
   constexpr uint32_t QBYTES = SUB * 128 * 128;
   constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kColO = 256;
   constexpr uint32_t ab_fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  constexpr uint32_t idesc_s = tc05::idesc_f16(ab_fmt, 128, 64, 0);
+  constexpr uint32_t idesc_s = tc05::idesc_f16(ab_fmt, 128, kBN, 0);
   constexpr uint32_t idesc_o = tc05::idesc_f16(ab_fmt, 128, D, 1);
 
   extern __shared__ uint8_t smem_raw[];
@@ -186,10 +177,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       mbar_init(&bars[kBarVFull + st], 1);
       mbar_init(&bars[kBarVEmpty + st], 1);
     }
-    for (int b = 0; b < kSBufs; ++b) mbar_init(&bars[kBarSFull + b], 1);
-    for (int b = 0; b < kPBufs; ++b) {
-      mbar_init(&bars[kBarPFull + b], 4);  // one arrival per warp of the owning warpgroup
-      mbar_init(&bars[kBarPvDone + b], 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&bars[kBarSFull + w], 1);
+      mbar_init(&bars[kBarPFull + w], 4);  // one arrival per warp of the warpgroup
+      mbar_init(&bars[kBarPvDone + w], 1);
     }
     mbar_init(&bars[kBarOEmpty], kSoftmaxWarps);
     mbar_init(&bars[kBarXchg], kSoftmaxWarps);
@@ -250,18 +241,18 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                                 &bars[kBarQFull], 0, sub, h * a.group + g, q_row0);
         }
         const int32_t* bt_row = a.bt + static_cast<int64_t>(s) * a.bt_stride;
-        const int n_kv = (kv_end + 63) / 64;
+        const int n_kv = (kv_end + kBN - 1) / kBN;
         bool ok = true;
-        // Cache rows of the next tile's four 16-row chunks, read one tile ahead so the
-        // block-table load latency overlaps the current tile's wait and TMA issue.  (fb, fw) =
-        // block index and row within the block of the next chunk; chunks past kv_end load
-        // (masked) rows of the sequence's first block.
+        // Cache rows of the next tile's 16-row chunks, read one tile ahead so the block-table
+        // load latency overlaps the current tile's wait and TMA issue.  (fb, fw) = block index
+        // and row within the block of the next chunk; chunks past kv_end load (masked) rows of
+        // the sequence's first block.
         int fb = 0, fw = 0;
-        int32_t nrow[4];
+        int32_t nrow[kChunks];
         auto fetch_rows = [&](int jj) {
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const bool real = jj * 64 + 16 * b < kv_end;
+          for (int b = 0; b < kChunks; ++b) {
+            const bool real = jj * kBN + 16 * b < kv_end;
             int32_t blk = bt_row[real ? fb : 0];
             if (blk < 0 || blk >= a.nb) {
               flag_status(a.status, B200_DEVICE_BAD_BLOCK);
@@ -279,9 +270,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         for (int j = 0; j < n_kv; ++j, ++kv_it) {
           const uint32_t st = kv_it % nst;
           const uint32_t ph = ((kv_it / nst) & 1u) ^ 1u;
-          int32_t rows[4];
+          int32_t rows[kChunks];
 #pragma unroll
-          for (int b = 0; b < 4; ++b) rows[b] = nrow[b];
+          for (int b = 0; b < kChunks; ++b) rows[b] = nrow[b];
           if (j + 1 < n_kv) fetch_rows(j + 1);
           if (!wait_or_abort(&empty[st], ph, abort_flag, a.status)) {
             ok = false;
@@ -290,10 +281,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           mbar_arrive_expect_tx(&full[st], KT);
           uint8_t* dst = ring + st * KT;
 #pragma unroll
-          for (int b = 0; b < 4; ++b)
+          for (int b = 0; b < kChunks; ++b)
 #pragma unroll
             for (int sub = 0; sub < SUB; ++sub)
-              tma_load_3d(dst + sub * 8192 + b * 2048, map, &full[st], 0, h * SUB + sub,
+              tma_load_3d(dst + sub * (kBN * 128) + b * 2048, map, &full[st], 0, h * SUB + sub,
                           rows[b]);
         }
         if (!ok) break;
@@ -315,51 +306,54 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       constexpr uint32_t kHi = tc05::desc_hi_sw128(1024);
       const uint32_t q_lo = tc05::desc_lo(base + L.q, 16);
       const uint32_t k_lo0 = tc05::desc_lo(base + L.k0, 16);
-      const uint32_t v_lo0 = tc05::desc_lo(base + L.v0, 8192);
-      const uint32_t p_lo0 = tc05::desc_lo(base + L.p, 16);
-      auto issue_s = [&](uint32_t slot, uint32_t stage) {
+      const uint32_t v_lo0 = tc05::desc_lo(base + L.v0, kBN * 128);  // LBO: next 64 columns
+      auto issue_s = [&](uint32_t wg, uint32_t stage) {
         const uint32_t k_lo = k_lo0 + stage * (KT >> 4);
-        const uint32_t d = tmem + slot * 64;
+        const uint32_t d = tmem + wg * kBN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
-          const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+          const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
           tc05::mma_f16(d, tc05::desc_join(q_lo + qo, kHi), tc05::desc_join(k_lo + ko, kHi),
                         idesc_s, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](uint32_t stage, uint32_t wg, bool acc) {
         const uint32_t v_lo = v_lo0 + stage * (KT >> 4);
-        const uint32_t p_lo = p_lo0 + wg * (16384 >> 4);
+        const uint32_t p_t = tmem + wg * kBN;  // P of this warpgroup: 2 values per column
         const uint32_t d = tmem + kColO + wg * D;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc05::mma_f16(d, tc05::desc_join(p_lo + kk * 2, kHi),
-                        tc05::desc_join(v_lo + kk * (2048 >> 4), kHi), idesc_o,
-                        (acc || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + kk * (2048 >> 4), kHi),
+                           idesc_o, (acc || kk > 0) ? 1u : 0u);
       };
-      auto issue_s_tile = [&](uint32_t g, uint32_t f) -> bool {  // S(g) from K fill f
+      // S(g) from K fill f.  S(g) overwrites the S/P buffer of warpgroup g % 2, whose P(g - 2) is
+      // read by PV(g - 2): that MMA must have completed first.
+      auto issue_s_tile = [&](uint32_t g, uint32_t f) -> bool {
+        const uint32_t wg = g & 1u;
+        if (g >= 2 &&
+            !wait_or_abort(&bars[kBarPvDone + wg], ((g - 2) >> 1) & 1u, abort_flag, a.status))
+          return false;
         if (!wait_or_abort(&bars[kBarKFull + f % kKStages], (f / kKStages) & 1u, abort_flag,
                            a.status))
           return false;
         tc05::fence_after_sync();
-        issue_s(g % kSBufs, f % kKStages);
-        tc05::commit(&bars[kBarSFull + g % kSBufs]);
+        issue_s(wg, f % kKStages);
+        tc05::commit(&bars[kBarSFull + wg]);
         tc05::commit(&bars[kBarKEmpty + f % kKStages]);
         return true;
       };
       for (int item = blockIdx.x; item < total; item += gridDim.x) {
         int s, h, q_row0, n_q, pos0, kv_end, ctx;
         decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
-        const int n_kv = (kv_end + 63) / 64;
+        const int n_kv = (kv_end + kBN - 1) / kBN;
         if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
         tc05::fence_after_sync();
         bool ok = true;
-        // the first S tiles of this item overlap the previous item's epilogue (S slots are free:
-        // every P of the previous item has been observed)
-        for (int j = 0; j < kSBufs && j < n_kv && ok; ++j) ok = issue_s_tile(s_it + j, kv_it + j);
+        // the first S tiles of this item overlap the previous item's epilogue
+        for (int j = 0; j < 2 && j < n_kv && ok; ++j) ok = issue_s_tile(s_it + j, kv_it + j);
         if (!ok) break;
-        if (n_kv <= kSBufs) tc05::commit(&bars[kBarQEmpty]);
+        if (n_kv <= 2) tc05::commit(&bars[kBarQEmpty]);
         // both O accumulators are free once all softmax warps have read the previous item's O
         if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
         tc05::fence_after_sync();
@@ -377,12 +371,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           issue_pv(f % kVStages, wg, j >= 2);  // tile j-2 went to the same accumulator
           tc05::commit(&bars[kBarPvDone + wg]);
           tc05::commit(&bars[kBarVEmpty + f % kVStages]);
-          if (j + kSBufs < n_kv) {
-            if (!issue_s_tile(g + kSBufs, f + kSBufs)) {
+          if (j + 2 < n_kv) {
+            if (!issue_s_tile(g + 2, f + 2)) {
               ok = false;
               break;
             }
-            if (j + kSBufs == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);  // last S of the item
+            if (j + 2 == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);  // last S of the item
           }
         }
         if (!ok) break;
@@ -404,6 +398,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const int g = row / a.tq;
     const int t = row - g * a.tq;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t s_self = trow + wg * kBN;
     const uint32_t o_self = trow + kColO + wg * D;
     const int sm_tid = (warp - 2 - 4 * static_cast<int>(wg)) * 32 + lane;  // 0..127
     float2* xch = reinterpret_cast<float2*>(smem + L.xch);
@@ -411,7 +406,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
       int s, h, q_row0, n_q, pos0, kv_end, ctx;
       decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
-      const int n_kv = (kv_end + 63) / 64;
+      const int n_kv = (kv_end + kBN - 1) / kBN;
       const bool valid = t < n_q;
       const int pos = valid ? pos0 + t : -1;
       // tiles of this warpgroup: j = j0, j0 + 2, ... (global tile number g = s_it + j, g % 2 == wg)
@@ -421,39 +416,32 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       int j = j0;
       for (; j < n_kv; j += 2) {
         const uint32_t gt = s_it + j;
-        ok = wait_or_abort(&bars[kBarSFull + gt % kSBufs], (gt / kSBufs) & 1u, abort_flag,
-                           a.status);
+        ok = wait_or_abort(&bars[kBarSFull + wg], (gt >> 1) & 1u, abort_flag, a.status);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
           break;
         }
         tc05::fence_after_sync();
-        float x[64];
-        {
-          float v0[32], v1[32];
-          tc05::ld_32x32b_x32(trow + (gt % kSBufs) * 64, v0);
-          tc05::ld_32x32b_x32(trow + (gt % kSBufs) * 64 + 32, v1);
-          tc05::wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            x[c] = v0[c];
-            x[32 + c] = v1[c];
-          }
-        }
         // causal mask only where some row of this warp ends inside the tile
-        const bool need_mask = __any_sync(0xffffffffu, j * 64 + 63 > pos);
-        if (need_mask) {
-          const int lim = pos - j * 64;  // columns c > lim are in the future of this row
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (c > lim) x[c] = -INFINITY;
-        }
-        // 8 independent partial maxima keep the dependent chains short
+        const bool need_mask = __any_sync(0xffffffffu, j * kBN + kBN - 1 > pos);
+        const int lim = pos - j * kBN;  // columns c > lim are in the future of this row
+        // pass 1: row max over the tile (32-column chunks)
         float mx8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = x[k];
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
-        for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], x[c]);
+        for (int c32 = 0; c32 < kBN / 32; ++c32) {
+          float v[32];
+          tc05::ld_32x32b_x32(s_self + c32 * 32, v);
+          tc05::wait_ld();
+          if (need_mask) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (c32 * 32 + c > lim) v[c] = -INFINITY;
+          }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], v[c]);
+        }
         const float smax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                  fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         // Online softmax with a lazily moved reference max: the row keeps using its current
@@ -469,27 +457,36 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           m = tmax;
         }
         const float mu = m == -INFINITY ? 0.f : m;
+        // pass 2: p = 2^(s*scale - m), packed in pairs and stored over the S columns this pass has
+        // already read (P chunk c covers S columns [32c, 32c + 32) and lands on [16c, 16c + 16))
         float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+        for (int c32 = 0; c32 < kBN / 32; ++c32) {
+          float x[32];
+          tc05::ld_32x32b_x32(s_self + c32 * 32, x);
+          tc05::wait_ld();
+          if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          x[c] = fast_exp2(fmaf(x[c], a.scale_log2, -mu));
-          rs8[c & 7] += x[c];
+            for (int c = 0; c < 32; ++c)
+              if (c32 * 32 + c > lim) x[c] = -INFINITY;
+          }
+          float pk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = fast_exp2(fmaf(x[c], a.scale_log2, -mu));
+            const float p1 = fast_exp2(fmaf(x[c + 1], a.scale_log2, -mu));
+            rs8[c & 7] += p0;
+            rs8[(c + 1) & 7] += p1;
+            pk[c >> 1] = __uint_as_float(MmaOp<T>::pack(p0, p1));
+          }
+          tc05::st_32x32b_x16(s_self + c32 * 16, pk);
         }
         const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
                          ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         l = l * alpha + rs;
-        if (gt >= 2) {
-          // this warpgroup's P buffer was last read by PV(gt - 2), which also is the last MMA
-          // into this warpgroup's O: after it completes, P may be overwritten and O rescaled
-          const uint32_t pg = gt - 2;
-          ok = wait_or_abort(&bars[kBarPvDone + wg], (pg >> 1) & 1u, abort_flag, a.status);
-          if (!__all_sync(0xffffffffu, ok)) {
-            ok = false;
-            break;
-          }
-        }
+        // O rescale: PV(gt - 2), the last MMA into this accumulator, completed before S(gt) was
+        // issued, so O can be read and written here
         if (j >= 2 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          tc05::fence_after_sync();
 #pragma unroll
           for (int ch = 0; ch < D / 16; ++ch) {
             float o[16];
@@ -499,9 +496,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             for (int c = 0; c < 16; ++c) o[c] *= alpha;
             tc05::st_32x32b_x16(o_self + ch * 16, o);
           }
-          tc05::wait_st();
         }
-        if (j == n_kv - 1 && kv_end < j * 64 + 64) {
+        tc05::wait_st();
+        if (j == n_kv - 1 && kv_end < j * kBN + kBN) {
           // keys past kv_end are masked for every row; their V rows may hold anything -> zero
           // (after the V tile has landed)
           const uint32_t fv = kv_it + j;
@@ -512,27 +509,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             break;
           }
           uint8_t* vst = smem + L.v0 + (fv % kVStages) * KT;
-          const int r0 = kv_end - j * 64;
-          const int nz = (64 - r0) * SUB * 8;  // 16-byte chunks
+          const int r0 = kv_end - j * kBN;
+          const int nz = (kBN - r0) * SUB * 8;  // 16-byte chunks
           for (int idx = sm_tid; idx < nz; idx += 128) {
             const int rr = r0 + idx / (SUB * 8);
             const int rem = idx % (SUB * 8);
-            *reinterpret_cast<uint4*>(vst + (rem >> 3) * 8192 + rr * 128 + (rem & 7) * 16) =
+            *reinterpret_cast<uint4*>(vst + (rem >> 3) * (kBN * 128) + rr * 128 + (rem & 7) * 16) =
                 make_uint4(0u, 0u, 0u, 0u);
           }
+          fence_proxy_async_smem();
         }
-        // P row (bf16/f16), 128B-swizzled K-major
-        uint8_t* pbuf = smem + L.p + wg * 16384;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint4 v;
-          v.x = MmaOp<T>::pack(x[c8 * 8 + 0], x[c8 * 8 + 1]);
-          v.y = MmaOp<T>::pack(x[c8 * 8 + 2], x[c8 * 8 + 3]);
-          v.z = MmaOp<T>::pack(x[c8 * 8 + 4], x[c8 * 8 + 5]);
-          v.w = MmaOp<T>::pack(x[c8 * 8 + 6], x[c8 * 8 + 7]);
-          *reinterpret_cast<uint4*>(pbuf + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
-        }
-        fence_proxy_async_smem();
         tc05::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc05::mbar_arrive(&bars[kBarPFull + wg]);

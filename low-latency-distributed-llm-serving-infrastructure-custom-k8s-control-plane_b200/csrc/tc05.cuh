@@ -83,6 +83,19 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+// Same MMA with the A operand (M x K, 16-bit, K-major) read from tensor memory: lane = row of A,
+// each 32-bit column holds two consecutive K elements (the lower half the even one), so one
+// K=16 step spans 8 columns starting at a_tmem.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 op this thread issued so far has completed.
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile(
