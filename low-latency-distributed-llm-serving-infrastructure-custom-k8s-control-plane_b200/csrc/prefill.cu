@@ -216,15 +216,19 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 
   if (warp == 0 || warp == 10) {
     // ------------------------------------------------------------------ TMA producers
-    if (lane == 0) {
+    // The whole warp runs the loop (warp-uniform coordinates); the elected lane issues.
+    {
+      const bool leader = elect_one_sync();
       const bool is_k = warp == 0;
       const CUtensorMap* map = is_k ? &kmap : &vmap;
       const uint32_t nst = is_k ? kKStages : kVStages;
       uint64_t* full = &bars[is_k ? kBarKFull : kBarVFull];
       uint64_t* empty = &bars[is_k ? kBarKEmpty : kBarVEmpty];
       uint8_t* ring = smem + (is_k ? L.k0 : L.v0);
-      if (is_k) prefetch_tensormap(&qmap);
-      prefetch_tensormap(map);
+      if (leader) {
+        if (is_k) prefetch_tensormap(&qmap);
+        prefetch_tensormap(map);
+      }
       const int32_t layer_base = a.layer * a.nb;
       uint32_t n_items = 0, kv_it = 0, q_issued = 0;
       for (int item = blockIdx.x; item < total; item += gridDim.x) {
@@ -233,12 +237,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         if (is_k) {
           if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
           ++q_issued;
-          mbar_arrive_expect_tx(&bars[kBarQFull], QBYTES);
-          for (int g = 0; g < a.group; ++g)
+          if (leader) {
+            mbar_arrive_expect_tx(&bars[kBarQFull], QBYTES);
+            for (int g = 0; g < a.group; ++g)
 #pragma unroll
-            for (int sub = 0; sub < SUB; ++sub)
-              tc05::tma_load_4d(smem + L.q + sub * 16384 + g * a.tq * 128, &qmap,
-                                &bars[kBarQFull], 0, sub, h * a.group + g, q_row0);
+              for (int sub = 0; sub < SUB; ++sub)
+                tc05::tma_load_4d(smem + L.q + sub * 16384 + g * a.tq * 128, &qmap,
+                                  &bars[kBarQFull], 0, sub, h * a.group + g, q_row0);
+          }
         }
         const int32_t* bt_row = a.bt + static_cast<int64_t>(s) * a.bt_stride;
         const int n_kv = (kv_end + kBN - 1) / kBN;
@@ -255,7 +261,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             const bool real = jj * kBN + 16 * b < kv_end;
             int32_t blk = bt_row[real ? fb : 0];
             if (blk < 0 || blk >= a.nb) {
-              flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+              if (leader) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
               blk = 0;
             }
             nrow[b] = (layer_base + blk) * a.bs + (real ? fw : 0);
@@ -278,14 +284,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[st], KT);
-          uint8_t* dst = ring + st * KT;
+          if (leader) {
+            mbar_arrive_expect_tx(&full[st], KT);
+            uint8_t* dst = ring + st * KT;
 #pragma unroll
-          for (int b = 0; b < kChunks; ++b)
+            for (int b = 0; b < kChunks; ++b)
 #pragma unroll
-            for (int sub = 0; sub < SUB; ++sub)
-              tma_load_3d(dst + sub * (kBN * 128) + b * 2048, map, &full[st], 0, h * SUB + sub,
-                          rows[b]);
+              for (int sub = 0; sub < SUB; ++sub)
+                tma_load_3d(dst + sub * (kBN * 128) + b * 2048, map, &full[st], 0,
+                            h * SUB + sub, rows[b]);
+          }
         }
         if (!ok) break;
         ++n_items;
@@ -299,7 +307,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop and waits (warp-uniform descriptors); the elected lane issues
+    // the MMAs and commits.
+    {
+      const bool leader = elect_one_sync();
       uint32_t n_items = 0, kv_it = 0, s_it = 0;
       // descriptor words built once; every MMA below adds a compile-time K-step offset and a
       // ring-stage offset to the low word
@@ -310,6 +321,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       auto issue_s = [&](uint32_t wg, uint32_t stage) {
         const uint32_t k_lo = k_lo0 + stage * (KT >> 4);
         const uint32_t d = tmem + wg * kBN;
+        if (!leader) return;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
@@ -322,6 +334,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const uint32_t v_lo = v_lo0 + stage * (KT >> 4);
         const uint32_t p_t = tmem + wg * kBN;  // P of this warpgroup: 2 values per column
         const uint32_t d = tmem + kColO + wg * D;
+        if (!leader) return;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + kk * (2048 >> 4), kHi),
@@ -339,8 +352,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           return false;
         tc05::fence_after_sync();
         issue_s(wg, f % kKStages);
-        tc05::commit(&bars[kBarSFull + wg]);
-        tc05::commit(&bars[kBarKEmpty + f % kKStages]);
+        if (leader) {
+          tc05::commit(&bars[kBarSFull + wg]);
+          tc05::commit(&bars[kBarKEmpty + f % kKStages]);
+        }
         return true;
       };
       for (int item = blockIdx.x; item < total; item += gridDim.x) {
@@ -353,7 +368,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         // the first S tiles of this item overlap the previous item's epilogue
         for (int j = 0; j < 2 && j < n_kv && ok; ++j) ok = issue_s_tile(s_it + j, kv_it + j);
         if (!ok) break;
-        if (n_kv <= 2) tc05::commit(&bars[kBarQEmpty]);
+        if (n_kv <= 2 && leader) tc05::commit(&bars[kBarQEmpty]);
         // both O accumulators are free once all softmax warps have read the previous item's O
         if (!wait_or_abort(&bars[kBarOEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
         tc05::fence_after_sync();
@@ -369,14 +384,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           }
           tc05::fence_after_sync();
           issue_pv(f % kVStages, wg, j >= 2);  // tile j-2 went to the same accumulator
-          tc05::commit(&bars[kBarPvDone + wg]);
-          tc05::commit(&bars[kBarVEmpty + f % kVStages]);
+          if (leader) {
+            tc05::commit(&bars[kBarPvDone + wg]);
+            tc05::commit(&bars[kBarVEmpty + f % kVStages]);
+          }
           if (j + 2 < n_kv) {
             if (!issue_s_tile(g + 2, f + 2)) {
               ok = false;
               break;
             }
-            if (j + 2 == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);  // last S of the item
+            if (j + 2 == n_kv - 1 && leader) tc05::commit(&bars[kBarQEmpty]);  // last S of item
           }
         }
         if (!ok) break;
@@ -384,8 +401,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         s_it += n_kv;
         ++n_items;
       }
-      // all tcgen05 work this thread issued completes before TMEM is released
-      tc05::commit(&bars[kBarFinal]);
+      // all tcgen05 work the leader issued completes before TMEM is released
+      if (leader) tc05::commit(&bars[kBarFinal]);
       mbar_wait_bounded(&bars[kBarFinal], 0);
     }
     __syncwarp();
