@@ -22,7 +22,8 @@
 //               TMEM when the row max moves.  The epilogue merges the two partial (O, max, sum)
 //               triples of each row, as a two-way split-KV combine, and writes O / l.
 // TMEM (512 columns): S/P of warpgroup w at columns [128w, 128w+128), O of warpgroup w at
-// [256 + w*D, 256 + (w+1)*D).  P(g) aliases S(g), so S(g+2) is issued only after PV(g) completed.
+// [256 + w*D, 256 + (w+1)*D).  P(g) aliases S(g); S(g+2) is issued right after PV(g) (in-order
+// tcgen05.mma execution orders PV(g)'s TMEM reads before S(g+2)'s writes).
 // Every mbarrier wait is bounded; an expired wait records B200_DEVICE_TIMEOUT and stops the CTA.
 #include <type_traits>
 
@@ -341,12 +342,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                            idesc_o, (acc || kk > 0) ? 1u : 0u);
       };
       // S(g) from K fill f.  S(g) overwrites the S/P buffer of warpgroup g % 2, whose P(g - 2) is
-      // read by PV(g - 2): that MMA must have completed first.
+      // the A operand of PV(g - 2).  S(g) is always issued after PV(g - 2) by this thread, and
+      // tcgen05.mma operations from one thread execute in issue order, so PV(g - 2) has read P
+      // before S(g) writes the buffer; no completion wait is needed.  (The commit after S(g) also
+      // covers PV(g - 2), so a warpgroup that sees S(g) may rescale its O.)
       auto issue_s_tile = [&](uint32_t g, uint32_t f) -> bool {
         const uint32_t wg = g & 1u;
-        if (g >= 2 &&
-            !wait_or_abort(&bars[kBarPvDone + wg], ((g - 2) >> 1) & 1u, abort_flag, a.status))
-          return false;
         if (!wait_or_abort(&bars[kBarKFull + f % kKStages], (f / kKStages) & 1u, abort_flag,
                            a.status))
           return false;
@@ -501,8 +502,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
                          ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         l = l * alpha + rs;
-        // O rescale: PV(gt - 2), the last MMA into this accumulator, completed before S(gt) was
-        // issued, so O can be read and written here
+        // O rescale: PV(gt - 2), the last MMA into this accumulator, was issued before S(gt) and
+        // is covered by the commit that signalled S(gt), so O can be read and written here
         if (j >= 2 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
           for (int ch = 0; ch < D / 16; ++ch) {
