@@ -597,8 +597,9 @@ def engine5_arm(args):
     g.manual_seed(7 + rank)
     for t in (kv.key_cache, kv.value_cache):
         t.normal_(generator=g)
-    # shuffled free list: fillers take the whole pool, released in random order
-    fillers = 64
+    # shuffled free list: fillers take the whole pool, released in random order (at least 64 of
+    # them, and enough that none exceeds a sequence's block-table row)
+    fillers = max(64, -(-blocks // pool.max_blocks_per_seq))
     per = blocks // fillers
     base_slot = pool.max_seqs - fillers
     for f in range(fillers):
