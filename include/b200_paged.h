@@ -202,6 +202,23 @@ int b200_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_st
                            int32_t layer_idx, const int64_t* slot_mapping, int32_t num_tokens,
                            int32_t* status_word, void* stream);
 
+/* Rotary embedding fused into the slot write.  Replaces the rotary step the model runs before
+ * the attention hook (transformers' apply_rotary_pos_emb, rotate-half form) together with
+ * scatter_layer_kv (app/model/paged_attention.py:150-152, app/memory/manager.py:150-168).
+ * qkv: (num_tokens, qkv_stride_token) rows laid out [q heads | k heads | v heads], each head
+ * head_dim contiguous elements of the cache dtype (the fused QKV projection output).
+ * positions: int64 per token; inv_freq: fp32 (head_dim/2,) rotary frequencies.
+ * Writes rotated q to q_out (num_tokens, num_query_heads, head_dim) with the given token stride,
+ * rotated k and unchanged v to the cache slots (slots < 0 skipped, >= NB*BS flag
+ * B200_DEVICE_BAD_SLOT).  Angles, cos/sin and the rotation are computed in fp32 with every
+ * product and sum rounded separately, bit-identical to the unfused elementwise path. */
+int b200_rope_reshape_and_cache(const void* qkv, int64_t qkv_stride_token, int32_t num_tokens,
+                                int32_t num_query_heads, const int64_t* positions,
+                                const float* inv_freq, void* q_out, int64_t q_out_stride_token,
+                                void* key_cache, void* value_cache, const B200CacheGeometry* geom,
+                                int32_t layer_idx, const int64_t* slot_mapping,
+                                int32_t* status_word, void* stream);
+
 /* ============================================================================================
  * 4. Device block pool (FIFO free list + per-sequence block tables resident on the GPU)
  * ==========================================================================================*/

@@ -89,6 +89,10 @@ SIGNATURES = [
     ("b200_reshape_and_cache", ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp,
                                               ctypes.POINTER(CacheGeometry), c_i32, c_vp, c_i32,
                                               c_vp, c_vp]),
+    ("b200_rope_reshape_and_cache", ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp,
+                                                   c_i64, c_vp, c_vp,
+                                                   ctypes.POINTER(CacheGeometry), c_i32, c_vp,
+                                                   c_vp, c_vp]),
     ("b200_pool_create", ctypes.c_int, [c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp)]),
     ("b200_pool_destroy", ctypes.c_int, [c_vp]),
     ("b200_pool_append_tokens", ctypes.c_int, [c_vp, c_i32, c_i32]),

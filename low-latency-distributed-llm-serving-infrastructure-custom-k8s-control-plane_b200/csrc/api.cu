@@ -655,4 +655,53 @@ int b200_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_st
   return B200_OK;
 }
 
+// ---- rotary + reshape_and_cache --------------------------------------------------------------
+
+int b200_rope_reshape_and_cache(const void* qkv, int64_t qkv_stride_token, int32_t num_tokens,
+                                int32_t num_query_heads, const int64_t* positions,
+                                const float* inv_freq, void* q_out, int64_t q_out_stride_token,
+                                void* key_cache, void* value_cache, const B200CacheGeometry* geom,
+                                int32_t layer_idx, const int64_t* slot_mapping,
+                                int32_t* status_word, void* stream) {
+  if (geom == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null geometry");
+  const B200CacheGeometry& g = *geom;
+  if (esize_of(g.dtype) == 0) return fail(B200_ERR_UNSUPPORTED, "unsupported dtype");
+  if (layer_idx < 0 || layer_idx >= g.num_layers)
+    return fail(B200_ERR_INVALID_ARGUMENT, "layer_idx out of range");
+  if (num_tokens < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_tokens < 0");
+  if (g.head_dim % 2 != 0 || g.head_dim > 1024)
+    return fail(B200_ERR_INVALID_ARGUMENT, "head_dim must be even and <= 1024");
+  if (num_query_heads <= 0 || num_query_heads % g.num_kv_heads != 0)
+    return fail(B200_ERR_INVALID_ARGUMENT, "num_query_heads must be a multiple of num_kv_heads");
+  if (qkv_stride_token < static_cast<int64_t>(num_query_heads + 2 * g.num_kv_heads) * g.head_dim)
+    return fail(B200_ERR_INVALID_ARGUMENT, "qkv_stride_token shorter than a q,k,v row");
+  if (q_out_stride_token < static_cast<int64_t>(num_query_heads) * g.head_dim)
+    return fail(B200_ERR_INVALID_ARGUMENT, "q_out_stride_token shorter than a q row");
+  if (num_tokens == 0) return B200_OK;
+  if (!qkv || !positions || !inv_freq || !q_out || !key_cache || !value_cache || !slot_mapping)
+    return fail(B200_ERR_INVALID_ARGUMENT, "null pointer");
+  b200::RopeCacheArgs a{};
+  a.qkv = qkv;
+  a.qkv_stok = qkv_stride_token;
+  a.hq = num_query_heads;
+  a.hkv = g.num_kv_heads;
+  a.head_dim = g.head_dim;
+  a.positions = positions;
+  a.inv_freq = inv_freq;
+  a.q_out = q_out;
+  a.q_stok = q_out_stride_token;
+  a.kc = key_cache;
+  a.vc = value_cache;
+  a.layer = layer_idx;
+  a.nb = g.total_blocks;
+  a.bs = g.block_size;
+  a.slots = slot_mapping;
+  a.num_tokens = num_tokens;
+  a.status = status_word;
+  cudaError_t e =
+      b200::launch_rope_cache(a, g.dtype, num_sms(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_reshape_and_cache");
+  return B200_OK;
+}
+
 }  // extern "C"

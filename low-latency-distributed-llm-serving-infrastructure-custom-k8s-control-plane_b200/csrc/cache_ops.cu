@@ -56,4 +56,86 @@ cudaError_t launch_reshape_and_cache(const CacheWriteArgs& a, int vec_bytes, int
   return cudaGetLastError();
 }
 
+// K2 with rotary embedding: the QKV projection output of a step goes in, the rotated queries come
+// out and the rotated keys and the values land in their cache slots -- in one pass instead of the
+// rotary elementwise ops (transformers' apply_rotary_pos_emb, run by the model before the
+// attention hook) followed by scatter_layer_kv (app/model/paged_attention.py:150-152,
+// app/memory/manager.py:150-168).
+//
+// Rotate-half rotary on (token, head) rows: with c = cos(pos * inv_freq[i]), s = sin(...) in fp32,
+//   y[i] = x[i]*c - x[i+D/2]*s,   y[i+D/2] = x[i+D/2]*c + x[i]*s,
+// each product and sum rounded separately, as the unfused elementwise ops round them, so the
+// result is bit-identical to that path.  One CTA per token: cos/sin of the token's D/2 angles are
+// computed once into shared memory and reused by all its q and k heads.
+template <typename T>
+__global__ void __launch_bounds__(128) rope_cache_kernel(RopeCacheArgs a) {
+  extern __shared__ float cs[];  // cos[0, D/2), sin[D/2, D)
+  const int half = a.head_dim / 2;
+  const int64_t slots_total = static_cast<int64_t>(a.nb) * a.bs;
+  const int rot_rows = a.hq + a.hkv;
+  for (int64_t t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {
+    __syncthreads();  // the previous token's angles are no longer read
+    const float pos = static_cast<float>(a.positions[t]);
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float ang = __fmul_rn(pos, a.inv_freq[i]);
+      cs[i] = cosf(ang);
+      cs[half + i] = sinf(ang);
+    }
+    __syncthreads();
+    const T* row = static_cast<const T*>(a.qkv) + t * a.qkv_stok;
+    const int64_t slot = a.slots[t];
+    const bool write_kv = slot >= 0 && slot < slots_total;
+    if (slot >= slots_total && threadIdx.x == 0) flag_status(a.status, B200_DEVICE_BAD_SLOT);
+    const int64_t cache_row =
+        write_kv ? ((static_cast<int64_t>(a.layer) * slots_total + slot) * a.hkv) : 0;
+    for (int w = threadIdx.x; w < rot_rows * half; w += blockDim.x) {
+      const int r = w / half;
+      const int i = w - r * half;
+      const T* src = row + static_cast<int64_t>(r) * a.head_dim;
+      const float x1 = to_f32<T>(src[i]);
+      const float x2 = to_f32<T>(src[i + half]);
+      const float c = cs[i], s = cs[half + i];
+      const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+      T* dst;
+      if (r < a.hq) {
+        dst = static_cast<T*>(a.q_out) + t * a.q_stok + static_cast<int64_t>(r) * a.head_dim;
+      } else if (write_kv) {
+        dst = static_cast<T*>(a.kc) + (cache_row + (r - a.hq)) * a.head_dim;
+      } else {
+        continue;
+      }
+      dst[i] = from_f32<T>(y1);
+      dst[i + half] = from_f32<T>(y2);
+    }
+    if (write_kv) {
+      const T* vsrc = row + static_cast<int64_t>(rot_rows) * a.head_dim;
+      T* vdst = static_cast<T*>(a.vc) + cache_row * a.head_dim;
+      for (int w = threadIdx.x; w < a.hkv * a.head_dim; w += blockDim.x) vdst[w] = vsrc[w];
+    }
+  }
+}
+
+cudaError_t launch_rope_cache(const RopeCacheArgs& a, int dtype, int num_sms, cudaStream_t stream) {
+  if (a.num_tokens <= 0) return cudaSuccess;
+  int64_t grid = a.num_tokens;
+  const int64_t cap = static_cast<int64_t>(num_sms > 0 ? num_sms : 148) * 16;
+  if (grid > cap) grid = cap;
+  const size_t smem = static_cast<size_t>(a.head_dim) * sizeof(float);
+  switch (dtype) {
+    case B200_DTYPE_BF16:
+      rope_cache_kernel<__nv_bfloat16><<<static_cast<int>(grid), 128, smem, stream>>>(a);
+      break;
+    case B200_DTYPE_F16:
+      rope_cache_kernel<__half><<<static_cast<int>(grid), 128, smem, stream>>>(a);
+      break;
+    case B200_DTYPE_F32:
+      rope_cache_kernel<float><<<static_cast<int>(grid), 128, smem, stream>>>(a);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace b200

@@ -21,6 +21,24 @@ struct CacheWriteArgs {
 cudaError_t launch_reshape_and_cache(const CacheWriteArgs& a, int vec_bytes, int num_sms,
                                      cudaStream_t stream);
 
+struct RopeCacheArgs {
+  const void* qkv;           // (tokens, (hq + 2*hkv) * D): q heads, then k heads, then v heads
+  int64_t qkv_stok;          // elements
+  int32_t hq, hkv, head_dim;
+  const int64_t* positions;  // (tokens,)
+  const float* inv_freq;     // (D/2,)
+  void* q_out;               // (tokens, hq, D), heads contiguous
+  int64_t q_stok;            // elements
+  void* kc;
+  void* vc;
+  int32_t layer, nb, bs;
+  const int64_t* slots;
+  int32_t num_tokens;
+  int32_t* status;
+};
+
+cudaError_t launch_rope_cache(const RopeCacheArgs& a, int dtype, int num_sms, cudaStream_t stream);
+
 // One queued block-pool op, uploaded as 4 int32.
 //   kind 0 = ALLOC:   append `count` blocks to slot's table starting at table index `first`
 //   kind 1 = RELEASE: free the slot's first `count` blocks in table order, clear the row

@@ -13,6 +13,12 @@ Differences that are the point of the rebuild: block allocation goes to the devi
 mixed forward, and sampling is a greedy argmax on the device with one host read per step
 (instead of one ``int(argmax)`` per sequence, llm_engine.py:200-204).
 
+Pure decode steps replay a CUDA graph captured per batch-size bucket (step metadata, the whole
+model forward with the fused rotary/cache-write and decode kernels, greedy sampling): the host
+work per step is the scheduler, one pool flush, two small pinned copies and the token read-back.
+Rows that pad a batch up to its bucket repeat the shortest real sequence; they recompute its
+token and write identical K/V bytes to the same slot, and their outputs are dropped.
+
 Tensor parallel runs: every rank runs the same engine on the same requests; scheduling is
 deterministic, the sampled tokens are identical on all ranks (vocab-parallel greedy over
 all-reduced hidden states), and rank 0's arrival decisions are broadcast each step, so every rank
@@ -20,6 +26,7 @@ takes the same collective steps in the same order.
 """
 from __future__ import annotations
 
+import ctypes
 import time
 from dataclasses import dataclass
 from enum import Enum
@@ -27,6 +34,7 @@ from typing import Dict, List, Optional
 
 import torch
 
+from . import _native as N
 from . import paged_ops
 from .kv_cache import PagedKVCacheManager
 
@@ -157,8 +165,29 @@ class Scheduler:
             self.waiting.remove(seq)
 
 
+# batch-size buckets of the captured decode graphs
+_GRAPH_BUCKETS = [1, 2, 4] + list(range(8, 257, 8)) + list(range(288, 2049, 32))
+
+
+class _DecodeGraph:
+    """Static buffers and the captured graph of one decode bucket (``rows`` sequences)."""
+
+    def __init__(self, rows: int, device: torch.device) -> None:
+        self.rows = rows
+        # rows of (sequence slot, start position, new-token count) and the input token ids
+        self.h_meta = torch.zeros((3, rows), dtype=torch.int32).pin_memory()
+        self.h_ids = torch.zeros(rows, dtype=torch.int64).pin_memory()
+        self.h_meta_np = self.h_meta.numpy()
+        self.h_ids_np = self.h_ids.numpy()
+        self.d_meta = torch.zeros((3, rows), dtype=torch.int32, device=device)
+        self.d_ids = torch.zeros(rows, dtype=torch.int64, device=device)
+        self.graph = torch.cuda.CUDAGraph()
+        self.out: Optional[torch.Tensor] = None
+
+
 class Engine:
-    def __init__(self, model, kv_cache_manager: PagedKVCacheManager, scheduler: Scheduler) -> None:
+    def __init__(self, model, kv_cache_manager: PagedKVCacheManager, scheduler: Scheduler,
+                 cuda_graphs: bool = True) -> None:
         self.model = model
         self.kv = kv_cache_manager
         self.scheduler = scheduler
@@ -168,6 +197,15 @@ class Engine:
         self.steps = 0
         self.tokens_generated = 0
         self.prefill_tokens = 0
+        self.graph_steps = 0
+        self.cuda_graphs = cuda_graphs
+        self._graphs: Dict[int, _DecodeGraph] = {}
+        self._graph_pool = None
+        self._graph_ws: Optional[torch.Tensor] = None
+        # decode graphs size their split plan and workspace for this context bound
+        self._ctx_bound = int(scheduler.max_model_len)
+        self._max_rows = next((b for b in _GRAPH_BUCKETS if b >= scheduler.max_batch_size),
+                              _GRAPH_BUCKETS[-1])
 
     def add_request(self, prompt_token_ids: List[int], max_tokens: int = 128,
                     eos_token_id: Optional[int] = None, arrival: float = 0.0) -> Sequence:
@@ -185,6 +223,27 @@ class Engine:
         seqs = out.scheduled_prefills + out.scheduled_decodes
         if not seqs:
             return {"finished": [], "running": []}
+        next_tokens = None
+        if self.cuda_graphs and not out.scheduled_prefills:
+            next_tokens = self._graph_decode(out.scheduled_decodes)
+        if next_tokens is None:
+            next_tokens = self._eager_step(out)
+        now = time.perf_counter()
+        for s, t in zip(seqs, next_tokens):
+            if s.first_token_time is None:
+                s.first_token_time = now
+            s.append_token(int(t))
+        self.tokens_generated += len(seqs)
+        self.steps += 1
+        finished = [s for s in seqs if s.is_finished()]
+        for s in finished:
+            s.finish_time = now
+            self.scheduler.free_sequence(s)
+        return {"finished": finished, "running": [s for s in seqs if not s.is_finished()]}
+
+    # ---- eager step (prefill or mixed batches) -------------------------------------------------
+    def _eager_step(self, out: SchedulerOutputs) -> List[int]:
+        seqs = out.scheduled_prefills + out.scheduled_decodes
         ids: List[int] = []
         starts: List[int] = []
         counts: List[int] = []
@@ -208,35 +267,115 @@ class Engine:
         bt, ctx, cu = md["block_tables"], md["context_lens"], md["cu_seqlens"]
         slots = md["slot_mapping"]
         scale = self.scale
+        positions = md["position_ids"]
+        inv_freq = self.model.inv_freq
+        hq = self.model.hq
 
-        def attend(layer, q, k, v):
-            paged_ops.reshape_and_cache(k, v, kc, vc, slots, layer)
+        def attend_qkv(layer, qkv):
+            # rotary + cache write in one kernel, then attention over the paged cache
+            q = paged_ops.rope_reshape_and_cache(qkv, positions, inv_freq, hq, kc, vc, slots,
+                                                 layer)
             if is_decode:
                 return paged_ops.paged_decode(q, kc, vc, layer, bt, ctx, scale, max_ctx)
             return paged_ops.paged_prefill(q, kc, vc, layer, bt, cu, ctx, scale, max_q, max_ctx)
 
         with torch.inference_mode():
-            hidden = self.model.forward(input_ids, md["position_ids"], attend)
+            hidden = self.model.forward(input_ids, positions, attend_qkv=attend_qkv)
             last = hidden.index_select(0, cu[1:] - 1)
-            next_tokens = self.model.greedy(last).cpu().tolist()
-        now = time.perf_counter()
-        for s, t in zip(seqs, next_tokens):
-            if s.first_token_time is None:
-                s.first_token_time = now
-            s.append_token(int(t))
-        self.tokens_generated += len(seqs)
-        self.steps += 1
-        finished = [s for s in seqs if s.is_finished()]
-        for s in finished:
-            s.finish_time = now
-            self.scheduler.free_sequence(s)
-        return {"finished": finished, "running": [s for s in seqs if not s.is_finished()]}
+            return self.model.greedy(last).cpu().tolist()
+
+    # ---- captured decode step --------------------------------------------------------------------
+    def _decode_body(self, g: _DecodeGraph) -> torch.Tensor:
+        """One decode step over g's static inputs: K4 metadata, forward, greedy (capturable: no
+        host synchronisation, fixed shapes and pointers)."""
+        pool = self.kv.pool
+        md = pool.build_step_metadata(g.d_meta[0], g.d_meta[1], g.d_meta[2], g.rows,
+                                      bt_stride=pool.max_blocks_per_seq)
+        positions, slots = md["position_ids"], md["slot_mapping"]
+        bt, ctx = md["block_tables"], md["context_lens"]
+        kc, vc = self.kv.key_cache, self.kv.value_cache
+        inv_freq, hq, scale = self.model.inv_freq, self.model.hq, self.scale
+        bound, ws = self._ctx_bound, self._graph_ws
+
+        def attend_qkv(layer, qkv):
+            q = paged_ops.rope_reshape_and_cache(qkv, positions, inv_freq, hq, kc, vc, slots,
+                                                 layer)
+            return paged_ops.paged_decode(q, kc, vc, layer, bt, ctx, scale, bound, workspace=ws)
+
+        hidden = self.model.forward(g.d_ids, positions, attend_qkv=attend_qkv)
+        return self.model.greedy(hidden)
+
+    def _graph_workspace(self) -> torch.Tensor:
+        """Decode workspace shared by every captured graph (graphs never run concurrently), sized
+        once for the largest bucket at the context bound so no capture ever reallocates it."""
+        if self._graph_ws is None:
+            L = N.lib()
+            kc = self.kv.key_cache
+            q = torch.empty((self._max_rows, self.model.hq, kc.shape[-1]), dtype=kc.dtype,
+                            device=self.device)
+            bt = torch.empty((self._max_rows, self.kv.pool.max_blocks_per_seq),
+                             dtype=torch.int32, device=self.device)
+            ctx = torch.empty(self._max_rows, dtype=torch.int32, device=self.device)
+            p = paged_ops.decode_params(q, kc, self.kv.value_cache, 0, bt, ctx, self.scale, q,
+                                        self._ctx_bound, None,
+                                        paged_ops.status_word(self.device))
+            need = int(L.b200_paged_decode_workspace_bytes(ctypes.byref(p)))
+            self._graph_ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+        return self._graph_ws
+
+    def _graph_decode(self, decodes: List[Sequence]) -> Optional[List[int]]:
+        B = len(decodes)
+        rows = next((b for b in _GRAPH_BUCKETS if b >= B), None)
+        if rows is None or rows > self._max_rows:
+            return None
+        g = self._graphs.get(rows)
+        fresh = g is None
+        if fresh:
+            g = _DecodeGraph(rows, self.device)
+        tokens = [s.block_table.get_tokens_count() for s in decodes]
+        donor = min(range(B), key=lambda i: tokens[i])  # pad rows repeat the shortest sequence
+        m, ids = g.h_meta_np, g.h_ids_np
+        for i, s in enumerate(decodes):
+            m[0, i] = s.block_table.slot
+            m[1, i] = tokens[i] - 1
+            ids[i] = s.output_token_ids[-1] if s.output_token_ids else s.prompt_token_ids[-1]
+        m[0, B:] = m[0, donor]
+        m[1, B:] = m[1, donor]
+        m[2, :] = 1
+        ids[B:] = ids[donor]
+        self.kv.pool.flush()  # this step's slot allocations, before the metadata kernel reads them
+        g.d_meta.copy_(g.h_meta, non_blocking=True)
+        g.d_ids.copy_(g.h_ids, non_blocking=True)
+        if fresh:
+            self._capture(g)
+        g.graph.replay()
+        self.graph_steps += 1
+        return g.out[:B].cpu().tolist()
+
+    def _capture(self, g: _DecodeGraph) -> None:
+        """Warm up on a side stream, then capture.  The warm-up runs execute this step's decode on
+        its real inputs; repeating it is idempotent (same K/V bytes to the same slots) and the
+        replay that follows produces the step's tokens."""
+        self._graph_workspace()
+        dev = self.device
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side), torch.inference_mode():
+            for _ in range(2):
+                self._decode_body(g)
+        cur.wait_stream(side)
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        with torch.inference_mode(), torch.cuda.graph(g.graph, pool=self._graph_pool):
+            g.out = self._decode_body(g)
+        self._graphs[g.rows] = g
 
 
 def build_engine(shape, total_blocks: int, block_size: int = 16, rank: int = 0, world: int = 1,
                  device=None, dtype=torch.bfloat16, seed: int = 0, max_batch_size: int = 256,
                  max_num_batched_tokens: int = 16384, max_model_len: int = 8192,
-                 full_init: bool = False, group=None) -> Engine:
+                 full_init: bool = False, group=None, cuda_graphs: bool = True) -> Engine:
     from .model import TPLlama
     device = torch.device(device or "cuda")
     model = TPLlama(shape, rank, world, device, dtype, seed, full_init=full_init, group=group)
@@ -246,4 +385,4 @@ def build_engine(shape, total_blocks: int, block_size: int = 16, rank: int = 0, 
                              device=device, max_seqs=max(16 * max_batch_size, 4096),
                              max_blocks_per_seq=max_blocks)
     sched = Scheduler(kv, max_batch_size, max_num_batched_tokens, max_model_len)
-    return Engine(model, kv, sched)
+    return Engine(model, kv, sched, cuda_graphs=cuda_graphs)

@@ -128,23 +128,35 @@ class TPLlama:
     def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         return F.rms_norm(x, (x.shape[-1],), w, self.shape.rms_eps)
 
-    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, attend) -> torch.Tensor:
-        """input_ids, positions: (Ntok,) on the device.  ``attend(layer, q, k, v)`` writes the
-        layer's new K/V into the paged cache and returns attention output (Ntok, hq, D).
-        Returns the final hidden states (Ntok, hidden)."""
+    @property
+    def inv_freq(self) -> torch.Tensor:
+        """Rotary frequencies (head_dim/2,) fp32 on the device."""
+        return self._inv_freq
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, attend=None,
+                attend_qkv=None) -> torch.Tensor:
+        """input_ids, positions: (Ntok,) on the device.  Either ``attend(layer, q, k, v)`` gets
+        the rotated q/k and v, writes the layer's new K/V into the paged cache and returns the
+        attention output (Ntok, hq, D); or ``attend_qkv(layer, qkv)`` gets the raw QKV
+        projection rows (Ntok, (hq + 2*hkv) * D) and does rotary, cache write and attention
+        itself (the fused path).  Returns the final hidden states (Ntok, hidden)."""
         s = self.shape
         D = s.head_dim
-        ang = positions.float()[:, None] * self._inv_freq[None, :]
-        cos, sin = torch.cos(ang), torch.sin(ang)
+        if attend_qkv is None:
+            ang = positions.float()[:, None] * self._inv_freq[None, :]
+            cos, sin = torch.cos(ang), torch.sin(ang)
         h = F.embedding(input_ids, self.embed)
         nq, nkv = self.hq * D, self.hkv * D
         for li, L in enumerate(self.layers):
             x = self._norm(h, L["n1"])
             qkv = F.linear(x, L["wqkv"])
-            q = self._rope(qkv[:, :nq].view(-1, self.hq, D), cos, sin)
-            k = self._rope(qkv[:, nq:nq + nkv].view(-1, self.hkv, D), cos, sin)
-            v = qkv[:, nq + nkv:].view(-1, self.hkv, D)
-            o = attend(li, q, k, v)
+            if attend_qkv is not None:
+                o = attend_qkv(li, qkv)
+            else:
+                q = self._rope(qkv[:, :nq].view(-1, self.hq, D), cos, sin)
+                k = self._rope(qkv[:, nq:nq + nkv].view(-1, self.hkv, D), cos, sin)
+                v = qkv[:, nq + nkv:].view(-1, self.hkv, D)
+                o = attend(li, q, k, v)
             h = h + self._all_reduce(F.linear(o.reshape(-1, nq), L["wo"]))
             x = self._norm(h, L["n2"])
             gu = F.linear(x, L["wgu"])

@@ -61,9 +61,13 @@ _STATUS = {}
 
 
 def status_word(device: torch.device) -> torch.Tensor:
-    key = (device.type, device.index)
+    """The device status word the kernels flag (one per GPU; ``cuda`` without an index means
+    the current device, so it names the same word as ``cuda:<current>``)."""
+    device = torch.device(device)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (device.type, index)
     if key not in _STATUS:
-        _STATUS[key] = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[key] = torch.zeros(1, dtype=torch.int32, device=torch.device(device.type, index))
     return _STATUS[key]
 
 
@@ -178,6 +182,42 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_cache: torch.T
         value.stride(1), key_cache.data_ptr(), value_cache.data_ptr(), ctypes.byref(geom),
         int(layer_idx), slot_mapping.data_ptr(), slot_mapping.numel(),
         status_word(key.device).data_ptr(), _stream(key.device)))
+
+
+def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+                           num_query_heads: int, key_cache: torch.Tensor,
+                           value_cache: torch.Tensor, slot_mapping: torch.Tensor, layer_idx: int,
+                           q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Rotary embedding fused into the slot write (K2 with rotary).
+
+    qkv (Ntok, (Hq + 2*Hkv) * D) = the fused QKV projection output (rows [q | k | v], unit
+    stride inside a row); positions (Ntok,) int64; inv_freq (D/2,) fp32.  Rotated k and v go to
+    their cache slots; returns the rotated q as (Ntok, Hq, D) (written into ``q_out`` if given).
+    Bit-identical to rotate-half rotary in fp32 followed by ``reshape_and_cache``."""
+    _require_cuda(qkv, positions, inv_freq, key_cache, value_cache, slot_mapping)
+    geom = cache_geometry(key_cache)
+    if qkv.dtype != key_cache.dtype or value_cache.dtype != key_cache.dtype:
+        raise ValueError("qkv dtype must match the cache dtype")
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("qkv must be (tokens, row) with unit stride inside a row")
+    if positions.dtype != torch.int64 or slot_mapping.dtype != torch.int64:
+        raise ValueError("positions and slot_mapping must be int64")
+    if inv_freq.dtype != torch.float32 or not inv_freq.is_contiguous():
+        raise ValueError("inv_freq must be contiguous float32")
+    n = qkv.shape[0]
+    D = geom.head_dim
+    if qkv.shape[1] < (int(num_query_heads) + 2 * geom.num_kv_heads) * D:
+        raise ValueError("qkv rows shorter than the q, k and v heads")
+    if q_out is None:
+        q_out = torch.empty((n, num_query_heads, D), dtype=qkv.dtype, device=qkv.device)
+    if q_out.stride(2) != 1 or q_out.stride(1) != D:
+        raise ValueError("q_out must have contiguous heads")
+    N.check(N.lib().b200_rope_reshape_and_cache(
+        qkv.data_ptr(), qkv.stride(0), n, int(num_query_heads), positions.data_ptr(),
+        inv_freq.data_ptr(), q_out.data_ptr(), q_out.stride(0), key_cache.data_ptr(),
+        value_cache.data_ptr(), ctypes.byref(geom), int(layer_idx), slot_mapping.data_ptr(),
+        status_word(qkv.device).data_ptr(), _stream(qkv.device)))
+    return q_out
 
 
 def paged_attention_masked(query: torch.Tensor, key_cache: torch.Tensor,

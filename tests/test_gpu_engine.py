@@ -1,6 +1,7 @@
 """The continuous-batching engine on the GPU: greedy tokens against a dense recompute of the same
 random-init model (attention by plain torch over each sequence's full history), with and without
-recompute-preemption, fp32 (CUDA-core kernels) and bf16 (tensor-core kernels)."""
+recompute-preemption, fp32 (CUDA-core kernels) and bf16 (tensor-core kernels); the captured
+decode graphs against the eager step."""
 import pytest
 import torch
 
@@ -56,6 +57,28 @@ def test_engine_fp32_matches_dense_greedy(pkg):
             assert int(_dense_logits(eng.model, toks).argmax()) == t
             toks.append(t)
     assert eng.kv.pool.get_num_free_blocks() == 128
+    assert eng.graph_steps > 0  # the pure decode steps ran as captured graphs
+    assert pkg.paged_ops.read_status(torch.device("cuda")) == 0
+
+
+def test_engine_graph_decode_matches_eager(pkg):
+    """Captured decode graphs (bucketed batch sizes, padded rows) give the eager engine's tokens.
+    Output lengths differ per request, so the decode batch shrinks through several buckets."""
+    from llm_serving_b200.engine import build_engine
+    from llm_serving_b200.model import LlamaShape
+    shape = LlamaShape(2, 128, 8, 2, 32, 256, 300)
+    prompts = _prompts(11, shape.vocab, 21)
+    lens = [3, 20, 7, 30, 12, 25, 5, 16, 9, 28, 14]
+    toks = {}
+    for graphs in (False, True):
+        eng = build_engine(shape, total_blocks=128, block_size=16, dtype=torch.float32, seed=6,
+                           max_batch_size=16, max_model_len=256, full_init=True,
+                           cuda_graphs=graphs)
+        toks[graphs] = [s.output_token_ids for s in _run(eng, prompts, lens)]
+        assert (eng.graph_steps > 0) == graphs
+        if graphs:
+            assert len(eng._graphs) >= 3
+    assert toks[True] == toks[False]
     assert pkg.paged_ops.read_status(torch.device("cuda")) == 0
 
 
