@@ -540,6 +540,8 @@ def engine4_arm(args):
     ttft = [s.first_token_time - s.arrival for s in seqs if s.first_token_time]
     tpot = [(s.finish_time - s.first_token_time) / max(1, len(s.output_token_ids) - 1)
             for s in seqs if s.finish_time and s.first_token_time]
+    graph_steps = eng.graph_steps
+    eng.release_graphs()  # captured graphs hold NCCL calls: release before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -554,7 +556,7 @@ def engine4_arm(args):
                                "max 256 decoding sequences, random-init 16x2048 Llama",
                    "parallelism": f"tp{world}", "kv_pool_blocks": blocks},
         "elapsed_s": round(elapsed, 3), "output_tokens": out_tokens, "steps": eng.steps,
-        "preemptions": eng.scheduler.preemption_count,
+        "graph_steps": graph_steps, "preemptions": eng.scheduler.preemption_count,
         "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 2) if ttft else None,
         "tpot_ms_p50": round(1e3 * float(np.median(tpot)), 3) if tpot else None,
     }
@@ -636,8 +638,11 @@ def engine5_arm(args):
     ms = e0.elapsed_time(e1)
     toks = eng.tokens_generated - gen0
     tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+    graph_steps = eng.graph_steps
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    eng.release_graphs()  # captured graphs hold NCCL calls: release before the process group
+    if world > 1:
         dist.destroy_process_group()
     ms = float(tt.item())
     if rank != 0:
@@ -652,7 +657,8 @@ def engine5_arm(args):
                    "parallelism": f"tp{world} (KV heads)", "sequences": len(ctxs),
                    "sum_ctx": int(sum(ctxs)), "kv_pool_blocks_per_gpu": blocks,
                    "kv_gb_per_gpu": args.kv_gb},
-        "preemptions": eng.scheduler.preemption_count, "wall_s": round(wall, 3),
+        "preemptions": eng.scheduler.preemption_count, "graph_steps": graph_steps,
+        "wall_s": round(wall, 3),
     }
     print(json.dumps(line))
     return 0

@@ -218,6 +218,19 @@ class Engine:
     def has_unfinished_requests(self) -> bool:
         return self.scheduler.has_unfinished_sequences()
 
+    def release_graphs(self) -> None:
+        """Drop the captured decode graphs.  Under tensor parallelism they hold NCCL calls, and
+        a process group must not be destroyed while such a graph is alive (its teardown then
+        waits forever): call this before ``destroy_process_group``.  Decoding afterwards simply
+        captures again."""
+        torch.cuda.synchronize(self.device)
+        for g in self._graphs.values():
+            g.graph.reset()
+            g.out = None
+        self._graphs.clear()
+        self._graph_pool = None
+        self._graph_ws = None
+
     def step(self) -> Dict[str, List[Sequence]]:
         out = self.scheduler.schedule()
         seqs = out.scheduled_prefills + out.scheduled_decodes

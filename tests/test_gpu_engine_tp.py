@@ -1,6 +1,7 @@
 """Tensor-parallel engine on 2 GPUs (NCCL): KV heads split across ranks, all-reduce after o_proj
-and down_proj, vocab-parallel greedy.  The generated tokens must equal the single-GPU engine's
-on the same random-init model.  Skipped on boxes with fewer than 2 GPUs."""
+and down_proj, vocab-parallel greedy, decode steps as captured graphs holding the collectives.
+The generated tokens must equal the single-GPU engine's on the same random-init model.  Skipped
+on boxes with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -46,6 +47,8 @@ def _worker(rank, world, port, q):
         eng.step()
     if rank == 0:
         q.put([s.output_token_ids for s in seqs])
+    assert eng.graph_steps > 0
+    eng.release_graphs()  # graphs holding NCCL calls go before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
