@@ -664,6 +664,82 @@ def engine5_arm(args):
     return 0
 
 
+def swap_arm(args):
+    """Whole-block copies (K6) at config-5 block geometry (32 layers, block 16, 8 KV heads, D 128,
+    bf16: 1 MiB of K and 1 MiB of V per block): 512 blocks at random ids of a 2048-block device
+    cache move out to a page-locked host swap space, back in to other random ids, and between
+    device blocks.  GB/s = block bytes moved / CUDA-event time; the host-link reference is a
+    plain 1 GiB pinned cudaMemcpyAsync in each direction timed the same way; the device copy
+    counts read + write bytes against the measured HBM copy peak."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200 import paged_ops
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    Ln, nb_dev, nb_host, n = 32, 2048, 512, 512
+    shape = (Ln, nb_dev, 16, 8, 128)
+    kc = torch.randn(shape, device=dev).to(torch.bfloat16)
+    vc = torch.randn(shape, device=dev).to(torch.bfloat16)
+    hk = torch.empty((Ln, nb_host, 16, 8, 128), dtype=torch.bfloat16).pin_memory()
+    hv = torch.empty_like(hk).pin_memory()
+    g = torch.Generator().manual_seed(9)
+    perm = torch.randperm(nb_dev, generator=g).to(torch.int32)
+    dev_ids, dev_ids2 = perm[:n].to(dev), perm[n:2 * n].to(dev)  # disjoint: no block is both
+    # a source and a destination of one call
+    host_ids = torch.randperm(nb_host, generator=g)[:n].to(torch.int32).to(dev)
+    block_bytes = Ln * 16 * 8 * 128 * 2 * 2  # K + V, all layers
+    moved = n * block_bytes
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps  # ms
+
+    ms_out = timed(lambda: paged_ops.copy_blocks(kc, vc, hk, hv, dev_ids, host_ids))
+    ms_in = timed(lambda: paged_ops.copy_blocks(hk, hv, kc, vc, host_ids, dev_ids2))
+    ms_dd = timed(lambda: paged_ops.copy_blocks(kc, vc, kc, vc, dev_ids, dev_ids2))
+    # round trip: the swapped-in (and then device-copied) blocks equal the swapped-out ones
+    ok = bool(torch.equal(kc[:, dev_ids2.long()].cpu(), hk[:, host_ids.long().cpu()]))
+    big_d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    big_h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    ms_d2h = timed(lambda: big_h.copy_(big_d, non_blocking=True))
+    ms_h2d = timed(lambda: big_d.copy_(big_h, non_blocking=True))
+    hbm, src = load_peaks()
+    gbs = lambda b, ms: round(b / (ms * 1e-3) / 1e9, 1)
+    line = {
+        "metric": "KV block swap GB/s (device -> host swap out)", "unit": "GB/s",
+        "value": gbs(moved, ms_out), "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "512 blocks of config-5 geometry (32 layers, BS 16, 8 KV heads, "
+                               "D 128; 2 MiB per block K+V) at random ids, 2048-block device "
+                               "cache, 512-block pinned host swap space",
+                   "bytes_per_call": moved},
+        "swap_in_gbs": gbs(moved, ms_in),
+        "device_copy_gbs": gbs(2 * moved, ms_dd),
+        "link_reference": {"d2h_memcpy_gbs": gbs(1 << 30, ms_d2h),
+                           "h2d_memcpy_gbs": gbs(1 << 30, ms_h2d)},
+        "roofline": {"swap_out_frac_of_link": round((moved / ms_out) / ((1 << 30) / ms_d2h), 3),
+                     "swap_in_frac_of_link": round((moved / ms_in) / ((1 << 30) / ms_h2d), 3),
+                     "device_copy_frac_of_hbm": round(gbs(2 * moved, ms_dd) / hbm, 3),
+                     "hbm_peak_gbs": hbm, "peak_source": src},
+        "round_trip_bit_exact": ok, "gpu_launches": 3 * args.steps,
+        "device_status": paged_ops.read_status(dev),
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -674,7 +750,7 @@ def main():
     ap.add_argument("--split", type=int, default=0, help="decode split tokens (0 = heuristic)")
     ap.add_argument("--cpu-seqs", type=int, default=32)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5"],
+    ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap"],
                     default="config2")
     ap.add_argument("--requests", type=int, default=200, help="engine4: requests to run")
     ap.add_argument("--rate", type=float, default=20.0, help="engine4: arrivals per second")
@@ -686,6 +762,8 @@ def main():
         return engine4_arm(args)
     if args.workload == "engine5":
         return engine5_arm(args)
+    if args.workload == "swap":
+        return swap_arm(args)
     if args.impl == "reference":
         return reference_arm(args)
     return ours_arm(args)

@@ -219,6 +219,25 @@ int b200_rope_reshape_and_cache(const void* qkv, int64_t qkv_stride_token, int32
                                 int32_t layer_idx, const int64_t* slot_mapping,
                                 int32_t* status_word, void* stream);
 
+/* Whole-block copy between two KV caches with the same layers, block size, heads, head_dim and
+ * dtype (their block counts may differ).  Replaces CudaKVCacheStrategy.copy_blocks
+ * (app/memory/strategies.py:117-122): pair i copies block src_blocks[i] of every layer of the
+ * source K and V caches into block dst_blocks[i] of the destination.  Either cache may be
+ * device memory or page-locked host memory (cudaHostAlloc / torch pin_memory, which the device
+ * addresses directly), so the same call moves blocks out to a host swap space, back in, or
+ * between device blocks (a copy before writing a shared block).  The two value caches may both
+ * be NULL to copy the key caches only (a single-cache copy).  The id arrays must be readable by
+ * the device; pageable host memory anywhere is rejected with B200_ERR_INVALID_ARGUMENT.  Pairs
+ * run in parallel: within one call no block may be both a destination and a source.  Ids
+ * outside a side's pool flag B200_DEVICE_BAD_BLOCK and that pair is skipped.  The bookkeeping of
+ * which block went where stays with the allocator (PageAllocator::swap_out / swap_in /
+ * share_block, page_allocator.hpp:142-241). */
+int b200_copy_blocks(const void* src_key_cache, const void* src_value_cache,
+                     const B200CacheGeometry* src_geom, void* dst_key_cache,
+                     void* dst_value_cache, const B200CacheGeometry* dst_geom,
+                     const int32_t* src_blocks, const int32_t* dst_blocks, int32_t num_blocks,
+                     int32_t* status_word, void* stream);
+
 /* ============================================================================================
  * 4. Device block pool (FIFO free list + per-sequence block tables resident on the GPU)
  * ==========================================================================================*/

@@ -93,6 +93,9 @@ SIGNATURES = [
                                                    c_i64, c_vp, c_vp,
                                                    ctypes.POINTER(CacheGeometry), c_i32, c_vp,
                                                    c_vp, c_vp]),
+    ("b200_copy_blocks", ctypes.c_int, [c_vp, c_vp, ctypes.POINTER(CacheGeometry), c_vp, c_vp,
+                                        ctypes.POINTER(CacheGeometry), c_vp, c_vp, c_i32, c_vp,
+                                        c_vp]),
     ("b200_pool_create", ctypes.c_int, [c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp)]),
     ("b200_pool_destroy", ctypes.c_int, [c_vp]),
     ("b200_pool_append_tokens", ctypes.c_int, [c_vp, c_i32, c_i32]),

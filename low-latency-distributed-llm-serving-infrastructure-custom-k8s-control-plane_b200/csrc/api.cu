@@ -704,4 +704,95 @@ int b200_rope_reshape_and_cache(const void* qkv, int64_t qkv_stride_token, int32
   return B200_OK;
 }
 
+// ---- whole-block copy (swap out / swap in / copy before write) -------------------------------
+
+namespace {
+// The address the device uses for p: device and managed memory as is, page-locked host memory
+// through its device mapping.  Pageable host memory (not reachable from the GPU) is rejected
+// here, so no kernel is ever given it.
+bool device_address(const void* p, const void** out) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  switch (at.type) {
+    case cudaMemoryTypeDevice:
+    case cudaMemoryTypeManaged:
+      *out = p;
+      return true;
+    case cudaMemoryTypeHost:
+      if (at.devicePointer == nullptr) return false;
+      // p may point inside the registered range: keep its offset
+      *out = static_cast<const char*>(at.devicePointer) +
+             (static_cast<const char*>(p) - static_cast<const char*>(at.hostPointer));
+      return true;
+    default:
+      return false;
+  }
+}
+}  // namespace
+
+int b200_copy_blocks(const void* src_key_cache, const void* src_value_cache,
+                     const B200CacheGeometry* src_geom, void* dst_key_cache,
+                     void* dst_value_cache, const B200CacheGeometry* dst_geom,
+                     const int32_t* src_blocks, const int32_t* dst_blocks, int32_t num_blocks,
+                     int32_t* status_word, void* stream) {
+  if (src_geom == nullptr || dst_geom == nullptr)
+    return fail(B200_ERR_INVALID_ARGUMENT, "null geometry");
+  const B200CacheGeometry& s = *src_geom;
+  const B200CacheGeometry& d = *dst_geom;
+  if (s.num_layers != d.num_layers || s.block_size != d.block_size ||
+      s.num_kv_heads != d.num_kv_heads || s.head_dim != d.head_dim || s.dtype != d.dtype)
+    return fail(B200_ERR_INVALID_ARGUMENT,
+                "source and destination caches differ in layers, block size, heads, head_dim or dtype");
+  const int es = esize_of(s.dtype);
+  if (es == 0) return fail(B200_ERR_UNSUPPORTED, "unsupported dtype");
+  if (num_blocks < 0) return fail(B200_ERR_INVALID_ARGUMENT, "num_blocks < 0");
+  if (num_blocks == 0) return B200_OK;
+  if (!src_key_cache || !dst_key_cache || !src_blocks || !dst_blocks)
+    return fail(B200_ERR_INVALID_ARGUMENT, "null pointer");
+  const bool with_v = src_value_cache != nullptr;
+  if (with_v != (dst_value_cache != nullptr))
+    return fail(B200_ERR_INVALID_ARGUMENT, "value caches must be both given or both null");
+  const void *sk, *dk, *sb, *db;
+  const void *sv = nullptr, *dv = nullptr;
+  if (!device_address(src_key_cache, &sk) || !device_address(dst_key_cache, &dk) ||
+      (with_v && (!device_address(src_value_cache, &sv) || !device_address(dst_value_cache, &dv))) ||
+      !device_address(src_blocks, &sb) || !device_address(dst_blocks, &db))
+    return fail(B200_ERR_INVALID_ARGUMENT,
+                "caches and block ids must be device memory or page-locked host memory");
+  src_key_cache = sk;
+  src_value_cache = sv;
+  dst_key_cache = const_cast<void*>(dk);
+  dst_value_cache = const_cast<void*>(dv);
+  src_blocks = static_cast<const int32_t*>(sb);
+  dst_blocks = static_cast<const int32_t*>(db);
+  b200::BlockCopyArgs a{};
+  a.src_k = src_key_cache;
+  a.src_v = src_value_cache;
+  a.dst_k = dst_key_cache;
+  a.dst_v = dst_value_cache;
+  a.layers = s.num_layers;
+  a.kv_count = with_v ? 2 : 1;
+  a.src_nb = s.total_blocks;
+  a.dst_nb = d.total_blocks;
+  a.block_bytes = static_cast<int64_t>(s.block_size) * s.num_kv_heads * s.head_dim * es;
+  a.src_blocks = src_blocks;
+  a.dst_blocks = dst_blocks;
+  a.num_blocks = num_blocks;
+  a.status = status_word;
+  const uint64_t align = static_cast<uint64_t>(a.block_bytes) |
+                         reinterpret_cast<uintptr_t>(src_key_cache) |
+                         reinterpret_cast<uintptr_t>(src_value_cache) |
+                         reinterpret_cast<uintptr_t>(dst_key_cache) |
+                         reinterpret_cast<uintptr_t>(dst_value_cache);  // null is aligned
+  int vec = 16;
+  while (vec > 2 && (align % vec) != 0) vec /= 2;
+  if (align % vec != 0) return fail(B200_ERR_INVALID_ARGUMENT, "misaligned cache pointers");
+  cudaError_t e = b200::launch_copy_blocks(a, vec, num_sms(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "copy_blocks");
+  return B200_OK;
+}
+
 }  // extern "C"

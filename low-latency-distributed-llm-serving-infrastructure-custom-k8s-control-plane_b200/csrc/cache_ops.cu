@@ -138,4 +138,57 @@ cudaError_t launch_rope_cache(const RopeCacheArgs& a, int dtype, int num_sms, cu
   return cudaGetLastError();
 }
 
+// K6: whole-block copy between two caches of the same per-block geometry, for swapping blocks out
+// to and back from pinned host memory and for copying a shared block before it is written
+// (CudaKVCacheStrategy.copy_blocks, app/memory/strategies.py:117-122, which copies block by block
+// with one copy_ per block and then synchronises).  Pair i copies block src_blocks[i] of every
+// layer of K and V into block dst_blocks[i].  One block of one layer is BS*Hkv*D contiguous
+// elements; consecutive threads take consecutive 16-byte (or narrower) chunks of it, so either
+// side may be device memory or page-locked host memory mapped into the device address space (the
+// copy then streams over the host link).  Ids outside a side's pool set B200_DEVICE_BAD_BLOCK
+// and the pair is skipped.
+template <typename V>
+__global__ void __launch_bounds__(256) copy_blocks_kernel(BlockCopyArgs a) {
+  const int64_t chunks = a.block_bytes / static_cast<int64_t>(sizeof(V));
+  const int64_t per_pair = chunks * a.layers * a.kv_count;
+  const int64_t total = per_pair * a.num_blocks;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t pair = i / per_pair;
+    int64_t rem = i - pair * per_pair;
+    const int64_t kv = rem / (chunks * a.layers);
+    rem -= kv * chunks * a.layers;
+    const int64_t layer = rem / chunks;
+    const int64_t c = rem - layer * chunks;
+    const int32_t sb = a.src_blocks[pair];
+    const int32_t db = a.dst_blocks[pair];
+    if (sb < 0 || sb >= a.src_nb || db < 0 || db >= a.dst_nb) {
+      if (rem == 0 && kv == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+      continue;
+    }
+    const char* src = static_cast<const char*>(kv ? a.src_v : a.src_k) +
+                      (layer * a.src_nb + sb) * a.block_bytes;
+    char* dst = static_cast<char*>(kv ? a.dst_v : a.dst_k) + (layer * a.dst_nb + db) * a.block_bytes;
+    reinterpret_cast<V*>(dst)[c] = reinterpret_cast<const V*>(src)[c];
+  }
+}
+
+cudaError_t launch_copy_blocks(const BlockCopyArgs& a, int vec_bytes, int num_sms,
+                               cudaStream_t stream) {
+  if (a.num_blocks <= 0) return cudaSuccess;
+  const int64_t total = a.block_bytes / vec_bytes * a.layers * a.kv_count * a.num_blocks;
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(num_sms > 0 ? num_sms : 148) * 8;
+  if (blocks > cap) blocks = cap;
+  const int grid = static_cast<int>(blocks);
+  switch (vec_bytes) {
+    case 16: copy_blocks_kernel<uint4><<<grid, 256, 0, stream>>>(a); break;
+    case 8: copy_blocks_kernel<uint2><<<grid, 256, 0, stream>>>(a); break;
+    case 4: copy_blocks_kernel<uint32_t><<<grid, 256, 0, stream>>>(a); break;
+    case 2: copy_blocks_kernel<uint16_t><<<grid, 256, 0, stream>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace b200

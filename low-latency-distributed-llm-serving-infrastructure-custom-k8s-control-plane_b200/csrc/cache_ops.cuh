@@ -39,6 +39,24 @@ struct RopeCacheArgs {
 
 cudaError_t launch_rope_cache(const RopeCacheArgs& a, int dtype, int num_sms, cudaStream_t stream);
 
+struct BlockCopyArgs {
+  const void* src_k;
+  const void* src_v;
+  void* dst_k;
+  void* dst_v;
+  int32_t layers;
+  int32_t kv_count;             // 2: K and V; 1: K only (single-cache copy)
+  int32_t src_nb, dst_nb;       // blocks per layer of each side
+  int64_t block_bytes;          // BS * Hkv * D * element size
+  const int32_t* src_blocks;
+  const int32_t* dst_blocks;
+  int32_t num_blocks;
+  int32_t* status;
+};
+
+cudaError_t launch_copy_blocks(const BlockCopyArgs& a, int vec_bytes, int num_sms,
+                               cudaStream_t stream);
+
 // One queued block-pool op, uploaded as 4 int32.
 //   kind 0 = ALLOC:   append `count` blocks to slot's table starting at table index `first`
 //   kind 1 = RELEASE: free the slot's first `count` blocks in table order, clear the row

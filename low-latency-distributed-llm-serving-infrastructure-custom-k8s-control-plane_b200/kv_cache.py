@@ -230,3 +230,74 @@ class PagedKVCacheManager:
         token_index = seq.block_table.get_tokens_count() - 1
         slot_mapping = self.build_slot_mapping([seq], [token_index], [1])
         self.scatter_kv(key_token.unsqueeze(0), value_token.unsqueeze(0), slot_mapping)
+
+    # ---- block copies (strategies.py:117-122) -------------------------------------------------
+    def copy_blocks(self, src_blocks, dst_blocks) -> None:
+        """Copy device blocks ``src_blocks[i] -> dst_blocks[i]`` (every layer, K and V) -- the
+        copy a caller makes before writing a block it shares with another sequence
+        (PageAllocator::share_block / SequenceBlockTable::replace_block,
+        csrc/include/page_allocator.hpp:142-149, :416-424).  Asynchronous on the current stream."""
+        paged_ops.copy_blocks(self.key_cache, self.value_cache, self.key_cache, self.value_cache,
+                              src_blocks, dst_blocks, device=self._device)
+
+
+class HostSwapSpace:
+    """Page-locked host blocks with the device cache's per-block layout: the swap space behind
+    PageAllocator::swap_out / swap_in (csrc/include/page_allocator.hpp:179-241), which keep only
+    the bookkeeping of which device block went to which host block.  The data moves with one
+    kernel per call (K6), the device reading or writing the pinned host memory directly over the
+    host link; calls are asynchronous on the current stream of the cache's device."""
+
+    def __init__(self, manager: PagedKVCacheManager, num_blocks: int) -> None:
+        L, _, BS, H, D = manager.key_cache.shape
+        shape = (L, int(num_blocks), BS, H, D)
+        self.manager = manager
+        self.key_cache = torch.empty(shape, dtype=manager.dtype).pin_memory()
+        self.value_cache = torch.empty(shape, dtype=manager.dtype).pin_memory()
+
+    def swap_out(self, device_blocks, host_blocks) -> None:
+        """Device block ``device_blocks[i]`` -> host block ``host_blocks[i]``."""
+        m = self.manager
+        paged_ops.copy_blocks(m.key_cache, m.value_cache, self.key_cache, self.value_cache,
+                              device_blocks, host_blocks, device=m.torch_device)
+
+    def swap_in(self, host_blocks, device_blocks) -> None:
+        """Host block ``host_blocks[i]`` -> device block ``device_blocks[i]``."""
+        m = self.manager
+        paged_ops.copy_blocks(self.key_cache, self.value_cache, m.key_cache, m.value_cache,
+                              host_blocks, device_blocks, device=m.torch_device)
+
+    def sync(self) -> None:
+        torch.cuda.current_stream(self.manager.torch_device).synchronize()
+
+
+class CudaKVCacheStrategy:
+    """The reference's CUDA cache strategy (app/memory/strategies.py:100-129) over this
+    library: same methods; ``copy_blocks`` moves block ``bid`` of every layer for each id in
+    ``physical_blocks`` with one kernel instead of one ``copy_`` per block.  Block ids index the
+    block dimension (dim 1) of the (L, NB, BS, Hkv, D) layout."""
+
+    def __init__(self, device_id: int = 0) -> None:
+        self._device = torch.device(f"cuda:{device_id}")
+
+    @property
+    def device(self) -> torch.device:
+        return self._device
+
+    def allocate_cache(self, total_blocks, block_size, num_layers, num_heads, head_dim, dtype):
+        shape = (num_layers, total_blocks, block_size, num_heads, head_dim)
+        return (torch.empty(shape, dtype=dtype, device=self._device),
+                torch.empty(shape, dtype=dtype, device=self._device))
+
+    def copy_blocks(self, src_cache: torch.Tensor, dst_cache: torch.Tensor,
+                    physical_blocks) -> None:
+        paged_ops.copy_blocks(src_cache, None, dst_cache, None, physical_blocks,
+                              physical_blocks, device=self._device)
+        self.sync()
+
+    def sync(self) -> None:
+        torch.cuda.current_stream(self._device).synchronize()
+
+    @property
+    def requires_copy_on_swap(self) -> bool:
+        return True

@@ -220,6 +220,50 @@ def rope_reshape_and_cache(qkv: torch.Tensor, positions: torch.Tensor, inv_freq:
     return q_out
 
 
+def _block_ids(ids, device: torch.device) -> torch.Tensor:
+    if isinstance(ids, torch.Tensor):
+        t = ids.to(dtype=torch.int32)
+        if t.is_cuda or t.is_pinned():
+            return t.contiguous()
+        return t.contiguous().to(device)
+    return torch.tensor(list(ids), dtype=torch.int32, device=device)
+
+
+def copy_blocks(src_key_cache: torch.Tensor, src_value_cache: Optional[torch.Tensor],
+                dst_key_cache: torch.Tensor, dst_value_cache: Optional[torch.Tensor],
+                src_blocks, dst_blocks, device: Optional[torch.device] = None) -> None:
+    """Copy whole blocks (every layer) between two caches of the same per-block geometry (K6):
+    block ``src_blocks[i]`` of the source K (and V) caches -> block ``dst_blocks[i]`` of the
+    destination.  Caches are (L, NB, BS, Hkv, D) tensors on the GPU or in page-locked host memory
+    (``pin_memory``): GPU -> host is a swap out, host -> GPU a swap in, GPU -> GPU the copy made
+    before writing a shared block.  The value caches may both be None (key caches only).
+    Asynchronous on the current stream of ``device`` (default: the GPU side's device)."""
+    caches = [t for t in (src_key_cache, src_value_cache, dst_key_cache, dst_value_cache)
+              if t is not None]
+    for t in caches:
+        if not (t.is_cuda or t.is_pinned()):
+            raise ValueError("caches must be on the GPU or in page-locked host memory")
+    if (src_value_cache is None) != (dst_value_cache is None):
+        raise ValueError("value caches must be both given or both None")
+    gpu = [t.device for t in caches if t.is_cuda]
+    dev = torch.device(device) if device is not None else (gpu[0] if gpu else
+                                                            torch.device("cuda"))
+    sg, dg = cache_geometry(src_key_cache), cache_geometry(dst_key_cache)
+    for a, b in ((src_value_cache, src_key_cache), (dst_value_cache, dst_key_cache)):
+        if a is not None and a.shape != b.shape:
+            raise ValueError("key and value caches of one side must have the same shape")
+    s_ids, d_ids = _block_ids(src_blocks, dev), _block_ids(dst_blocks, dev)
+    if s_ids.numel() != d_ids.numel():
+        raise ValueError("src_blocks and dst_blocks must have the same length")
+    with torch.cuda.device(dev):
+        N.check(N.lib().b200_copy_blocks(
+            src_key_cache.data_ptr(), None if src_value_cache is None else src_value_cache.data_ptr(),
+            ctypes.byref(sg), dst_key_cache.data_ptr(),
+            None if dst_value_cache is None else dst_value_cache.data_ptr(), ctypes.byref(dg),
+            s_ids.data_ptr(), d_ids.data_ptr(), s_ids.numel(), status_word(dev).data_ptr(),
+            _stream(dev)))
+
+
 def paged_attention_masked(query: torch.Tensor, key_cache: torch.Tensor,
                            value_cache: torch.Tensor, layer_idx: int, gather_slots: torch.Tensor,
                            attention_mask: torch.Tensor, scaling: float) -> torch.Tensor:
