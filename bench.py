@@ -143,9 +143,9 @@ def cpu_sample_inputs(b, nseq, seed=1):
     return seqs
 
 
-def run_cpu_kernel(b, seqs, repeats=1):
-    """Time the reference kernel (or the oracle port) over the sample; returns
-    (GB/s, seconds, kind, cores)."""
+def run_cpu_kernel(b, seqs, repeats=1, min_seconds=0.0):
+    """Time the reference kernel (or the oracle port) over the sample, `repeats` passes or as many
+    as fill `min_seconds`; returns (GB/s, seconds per pass, kind, cores, passes)."""
     from oracle import oracle as O
     cores = os.cpu_count() or 1
     if O.RefKernel.available():
@@ -160,11 +160,13 @@ def run_cpu_kernel(b, seqs, repeats=1):
         ctx = gs.shape[0]
         nbytes += ctx * b.num_kv_heads * b.head_dim * 2 * 2 + 2 * b.num_query_heads * b.head_dim * 2
     t0 = time.perf_counter()
-    for _ in range(repeats):
+    passes = 0
+    while passes < repeats or time.perf_counter() - t0 < min_seconds:
         for q, kc, vc, gs, mask in seqs:
             call(q, kc, vc, 0, gs, mask, b.scale)
+        passes += 1
     dt = time.perf_counter() - t0
-    return nbytes * repeats / dt / 1e9, dt / repeats, kind, cores
+    return nbytes * passes / dt / 1e9, dt / passes, kind, cores, passes
 
 
 def reference_arm(args):
@@ -180,7 +182,7 @@ def reference_arm(args):
         run_cpu_kernel(b, seqs[:4])
     vals, times = [], []
     for _ in range(args.steps):
-        v, dt, kind, cores = run_cpu_kernel(b, seqs)
+        v, dt, kind, cores, _ = run_cpu_kernel(b, seqs)
         vals.append(v)
         times.append(dt)
     value = statistics.median(vals)
@@ -278,44 +280,67 @@ def ours_arm(args):
     elapsed_ms = t0.elapsed_time(t1)
     decode_ms = sum(a.elapsed_time(c) for a, c in ev) / args.steps
 
-    # e2e through the public API with host buffers: H2D of the step's inputs, the kernels, D2H
-    # of the result, every step
-    h_q = q.cpu().pin_memory()
-    h_k = newk.cpu().pin_memory()
-    h_v = newv.cpu().pin_memory()
-    h_slots = slots.cpu().pin_memory()
-    h_bt = bt.cpu().pin_memory()
-    h_ctx = ctx.cpu().pin_memory()
-    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    d_q, d_k, d_v = torch.empty_like(q), torch.empty_like(newk), torch.empty_like(newv)
-    d_slots, d_bt, d_ctx = torch.empty_like(slots), torch.empty_like(bt), torch.empty_like(ctx)
-    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_bt, h_ctx))
-    d2h = h_out.numel() * h_out.element_size()
+    # e2e through the public API with host buffers: every step copies its inputs from pinned host
+    # memory and reads its result back, inside the timed region.  As a serving loop would, the
+    # copies run on a copy stream with two buffer sets: step i+1's inputs go up while step i
+    # decodes, and step i's output comes back while step i+1 computes.
+    h_in = {"q": q.cpu().pin_memory(), "k": newk.cpu().pin_memory(),
+            "v": newv.cpu().pin_memory(), "slots": slots.cpu().pin_memory(),
+            "bt": bt.cpu().pin_memory(), "ctx": ctx.cpu().pin_memory()}
+    h_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    bufs = [{n: torch.empty_like(t, device=dev) for n, t in h_in.items()} for _ in range(2)]
+    for bset in bufs:
+        bset["out"] = torch.empty_like(out)
+    h2d = sum(t.numel() * t.element_size() for t in h_in.values())
+    d2h = h_out[0].numel() * h_out[0].element_size()
+    copy = torch.cuda.Stream(dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        d_q.copy_(h_q, non_blocking=True)
-        d_k.copy_(h_k, non_blocking=True)
-        d_v.copy_(h_v, non_blocking=True)
-        d_slots.copy_(h_slots, non_blocking=True)
-        d_bt.copy_(h_bt, non_blocking=True)
-        d_ctx.copy_(h_ctx, non_blocking=True)
-        paged_ops.reshape_and_cache(d_k, d_v, kc, vc, d_slots, 0)
-        paged_ops.paged_decode(d_q, kc, vc, 0, d_bt, d_ctx, b.scale, max_ctx, out=out)
-        h_out.copy_(out, non_blocking=True)
+    def upload(i):
+        bset = bufs[i % 2]
+        with torch.cuda.stream(copy):
+            if i >= 2:
+                copy.wait_event(done[i % 2])  # step i-2 has finished with this buffer set
+            for n, t in h_in.items():
+                bset[n].copy_(t, non_blocking=True)
+            ready[i % 2].record(copy)
 
-    for _ in range(3):
-        e2e_step()
+    def compute(i):
+        bset = bufs[i % 2]
+        stream.wait_event(ready[i % 2])
+        paged_ops.reshape_and_cache(bset["k"], bset["v"], kc, vc, bset["slots"], 0)
+        paged_ops.paged_decode(bset["q"], kc, vc, 0, bset["bt"], bset["ctx"], b.scale, max_ctx,
+                               out=bset["out"])
+        done[i % 2].record(stream)
+
+    def download(i):
+        with torch.cuda.stream(copy):
+            copy.wait_event(done[i % 2])
+            h_out[i % 2].copy_(bufs[i % 2]["out"], non_blocking=True)
+
+    def e2e_run(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            compute(i)
+            download(i)
+        stream.wait_stream(copy)
+
+    e2e_run(3)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    copy.wait_stream(stream)
+    e2e_run(args.steps)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
+    e2e_ok = bool(torch.equal(h_out[(args.steps - 1) % 2], out.cpu()))
 
     times = torch.tensor([elapsed_ms, e2e_ms, decode_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -326,11 +351,12 @@ def ours_arm(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         seqs = cpu_sample_inputs(b, args.cpu_seqs)
-        v, dt, kind, cores = run_cpu_kernel(b, seqs)
+        run_cpu_kernel(b, seqs[:4])  # warm-up
+        v, dt, kind, cores, passes = run_cpu_kernel(b, seqs, min_seconds=args.cpu_seconds)
         cpu = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind,
                "sample": f"first {args.cpu_seqs} config-2 sequences (sum ctx "
                          f"{int(b.context_lens[:args.cpu_seqs].sum())}), one call per sequence, "
-                         f"bf16 values upcast to fp32; {dt:.2f} s"}
+                         f"bf16 values upcast to fp32; {passes} passes, {passes * dt:.1f} s"}
 
     if world > 1:
         dist.destroy_process_group()
@@ -359,7 +385,10 @@ def ours_arm(args):
                      "kernel": "b200_paged_decode (plan + decode_tc), bytes per launch %d"
                                % decode_bytes},
         "e2e": {"value": round(world * total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9, 2),
-                "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "pipelining": "copy stream, two buffer sets: inputs of step i+1 and output of "
+                              "step i-1 move while step i computes",
+                "output_matches_device_run": e2e_ok},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "device_status": status,
@@ -748,7 +777,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seqs", type=int, default=256)
     ap.add_argument("--split", type=int, default=0, help="decode split tokens (0 = heuristic)")
-    ap.add_argument("--cpu-seqs", type=int, default=32)
+    ap.add_argument("--cpu-seqs", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="minimum CPU work of the cpu_baseline leg (passes over the sample)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap"],
                     default="config2")
