@@ -103,8 +103,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base_u32 - raw_u32);
-  float* o_w = reinterpret_cast<float*>(smem + NW * NS * Cfg::kStage);     // [NW][8][OSTR]
-  float* m_w = o_w + NW * 8 * OSTR;                                          // [NW][8]
+  // Each warp's [8][OSTR] merge rows alias its own TMA stage region: the ring of a warp is
+  // drained (every fill consumed) before it writes them, and refilled only after the merge.
+  static_assert(8 * OSTR * 4 <= NS * Cfg::kStage, "merge rows must fit a warp's stage region");
+  auto o_w_of = [&](int w) { return reinterpret_cast<float*>(smem + w * NS * Cfg::kStage); };
+  float* m_w = reinterpret_cast<float*>(smem + NW * NS * Cfg::kStage);       // [NW][8]
   float* l_w = m_w + NW * 8;                                                 // [NW][8]
   uint64_t* bars = reinterpret_cast<uint64_t*>(l_w + NW * 8);                // [NW][NS]
   int32_t* item_s = reinterpret_cast<int32_t*>(bars + NW * NS);              // [4]
@@ -186,6 +189,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       }
     };
     if (lane == 0) {
+      // the stage region was last written and read through the generic proxy (merge rows,
+      // V zeroing): order that before the async-proxy fills
+      fence_proxy_async_smem();
       const int pre = min(NS, n_my);
       for (int j = 0; j < pre; ++j) issue(j, fill_it + j);
     }
@@ -329,7 +335,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
       const int d0 = 16 * mt + r;
-      float* ow = o_w + warp * 8 * OSTR;
+      float* ow = o_w_of(warp);
       ow[(2 * c) * OSTR + d0] = acc[mt][0];
       ow[(2 * c + 1) * OSTR + d0] = acc[mt][1];
       ow[(2 * c) * OSTR + d0 + 8] = acc[mt][2];
@@ -348,7 +354,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 #pragma unroll
       for (int w = 0; w < NW; ++w) {
         const float wt = fast_exp2(m_w[w * 8 + hh] - Mu);
-        o += wt * o_w[(w * 8 + hh) * OSTR + d];
+        o += wt * o_w_of(w)[hh * OSTR + d];
         L += wt * l_w[w * 8 + hh];
       }
       const float val = L > 0.f ? o / L : 0.f;
@@ -550,8 +556,8 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
 template <typename T, int D, int NS>
 static int decode_tc_smem_bytes() {
   using Cfg = TcTile<D>;
-  return 1024 + kDecodeWarps * NS * Cfg::kStage + kDecodeWarps * 8 * (D + 4) * 4 +
-         2 * kDecodeWarps * 8 * 4 + kDecodeWarps * NS * 8 + 16;
+  return 1024 + kDecodeWarps * NS * Cfg::kStage + 2 * kDecodeWarps * 8 * 4 +
+         kDecodeWarps * NS * 8 + 16;
 }
 
 template <typename T, int D, int NS>

@@ -7,7 +7,7 @@ namespace b200 {
 
 constexpr int kDecodeWarps = 4;
 constexpr int kDecodeThreads = 32 * kDecodeWarps;
-constexpr int kDecodeStages = 2;  // TMA ring depth per warp (2 CTAs per SM fit)
+constexpr int kDecodeStages = 3;  // TMA ring depth per warp (2 CTAs per SM fit)
 
 // Shared-memory tile of one 16-token unit: K then V, each D/64 sub-buffers of 16 rows x 128 B
 // (128B-swizzled, as TMA writes them).
