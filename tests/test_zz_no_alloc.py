@@ -57,8 +57,8 @@ def test_static_decode_rejects_batches_beyond_its_scratch(pkg):
                              num_query_heads=32, num_kv_heads=8, head_dim=128, block_size=16)
     q, kc, vc, bt, ctx = device_batch(b, torch.bfloat16, seed=1)
     out = torch.empty_like(q)
-    # a host bound of 2^20 tokens per sequence sizes the plan far past 64 MiB
-    p = paged_ops.decode_params(q, kc, vc, 0, bt, ctx, b.scale, out, 1 << 20)
+    # a host bound of 2^24 tokens per sequence sizes the plan far past 64 MiB
+    p = paged_ops.decode_params(q, kc, vc, 0, bt, ctx, b.scale, out, 1 << 24)
     need = _native.lib().b200_paged_decode_workspace_bytes(ctypes.byref(p))
     assert need > (64 << 20)
     with pytest.raises(ValueError, match="allocation-free decode holds"):
