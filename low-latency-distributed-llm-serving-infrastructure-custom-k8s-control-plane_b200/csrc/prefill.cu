@@ -21,9 +21,9 @@
 //               and stored with tcgen05.st over the S columns already consumed, rescale of O in
 //               TMEM when the row max moves.  The epilogue merges the two partial (O, max, sum)
 //               triples of each row, as a two-way split-KV combine, and writes O / l.
-// TMEM (512 columns): S/P of warpgroup w at columns [128w, 128w+128), O of warpgroup w at
-// [256 + w*D, 256 + (w+1)*D).  P(g) aliases S(g); S(g+2) is issued right after PV(g) (in-order
-// tcgen05.mma execution orders PV(g)'s TMEM reads before S(g+2)'s writes).
+// TMEM (512 columns): S/P of warpgroup w at columns [128w, 128w+128) (P in the upper 64), O of
+// warpgroup w at [256 + w*D, 256 + (w+1)*D).  P(g) aliases S(g); S(g+2) is issued right after
+// PV(g) (in-order tcgen05.mma execution orders PV(g)'s TMEM reads before S(g+2)'s writes).
 // Every mbarrier wait is bounded; an expired wait records B200_DEVICE_TIMEOUT and stops the CTA.
 #include <type_traits>
 
@@ -35,6 +35,9 @@ namespace b200 {
 namespace {
 
 constexpr int kBN = 128;  // keys per KV tile (the N of S = Q.K^T, the K of O += P.V)
+// P column group g (32 keys) of a tile holds key chunk kPChunk[g]: the softmax writes the chunks
+// still in registers after the row-max pass first (see the softmax warps).
+__device__ constexpr uint32_t kPChunk[4] = {2, 3, 0, 1};
 // K and V stream through separate rings: a K stage is released as soon as its S = Q.K^T has
 // completed, a V stage when its PV has.  K is needed before V, hence the deeper K ring.
 constexpr int kKStages = 3;
@@ -333,13 +336,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       };
       auto issue_pv = [&](uint32_t stage, uint32_t wg, bool acc) {
         const uint32_t v_lo = v_lo0 + stage * (KT >> 4);
-        const uint32_t p_t = tmem + wg * kBN;  // P of this warpgroup: 2 values per column
+        // P of this warpgroup: upper half of its S buffer, 2 values per column; column group g
+        // (two K=16 steps) holds keys of chunk kPChunk[g] (32 keys = two 16-row V steps)
+        const uint32_t p_t = tmem + wg * kBN + 64;
         const uint32_t d = tmem + kColO + wg * D;
         if (!leader) return;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + kk * (2048 >> 4), kHi),
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t vrow16 = kPChunk[kk >> 1] * 2 + (kk & 1);  // 16-key V step
+          tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + vrow16 * (2048 >> 4), kHi),
                            idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
       };
       // S(g) from K fill f.  S(g) overwrites the S/P buffer of warpgroup g % 2, whose P(g - 2) is
       // the A operand of PV(g - 2).  S(g) is always issued after PV(g - 2) by this thread, and
@@ -443,23 +450,37 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         // causal mask only where some row of this warp ends inside the tile
         const bool need_mask = __any_sync(0xffffffffu, j * kBN + kBN - 1 > pos);
         const int lim = pos - j * kBN;  // columns c > lim are in the future of this row
-        // pass 1: row max over the tile (32-column chunks)
-        float mx8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll
-        for (int c32 = 0; c32 < kBN / 32; ++c32) {
-          float v[32];
-          tc05::ld_32x32b_x32(s_self + c32 * 32, v);
-          tc05::wait_ld();
+        // pass 1: row max over the tile, two 64-column halves (one TMEM wait each); the second
+        // half stays in registers for pass 2
+        float va[32], vb[32];
+        auto mask_chunk = [&](float (&v)[32], int chunk) {
           if (need_mask) {
 #pragma unroll
             for (int c = 0; c < 32; ++c)
-              if (c32 * 32 + c > lim) v[c] = -INFINITY;
+              if (chunk * 32 + c > lim) v[c] = -INFINITY;
           }
+        };
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+        auto max_chunk = [&](const float (&v)[32]) {
 #pragma unroll
           for (int c = 0; c < 32; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], v[c]);
-        }
+        };
+        tc05::ld_32x32b_x32(s_self, va);
+        tc05::ld_32x32b_x32(s_self + 32, vb);
+        tc05::wait_ld();
+        mask_chunk(va, 0);
+        mask_chunk(vb, 1);
+        max_chunk(va);
+        max_chunk(vb);
+        tc05::ld_32x32b_x32(s_self + 64, va);
+        tc05::ld_32x32b_x32(s_self + 96, vb);
+        tc05::wait_ld();
+        mask_chunk(va, 2);
+        mask_chunk(vb, 3);
+        max_chunk(va);
+        max_chunk(vb);
         const float smax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                  fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         // Online softmax with a lazily moved reference max: the row keeps using its current
@@ -475,30 +496,35 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           m = tmax;
         }
         const float mu = m == -INFINITY ? 0.f : m;
-        // pass 2: p = 2^(s*scale - m), packed in pairs and stored over the S columns this pass has
-        // already read (P chunk c covers S columns [32c, 32c + 32) and lands on [16c, 16c + 16))
+        // pass 2: p = 2^(s*scale - m), packed in pairs into the upper half of the S buffer
+        // (columns 64..127).  Chunks 2 and 3 (still in registers) go first, onto their own
+        // consumed columns; then chunks 0 and 1 are re-read.  P column group g (16 columns = 32 keys)
+        // holds key chunk kPChunk[g] = 2, 3, 0, 1; the PV MMA reads V in the same order.
         float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-        for (int c32 = 0; c32 < kBN / 32; ++c32) {
-          float x[32];
-          tc05::ld_32x32b_x32(s_self + c32 * 32, x);
-          tc05::wait_ld();
-          if (need_mask) {
+        auto exp_chunk = [&](const float (&x)[32], int group) {
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (c32 * 32 + c > lim) x[c] = -INFINITY;
-          }
-          float pk[16];
+          for (int h = 0; h < 2; ++h) {  // two 16-key halves, 8 packed columns each
+            float pk[8];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const float p0 = fast_exp2(fmaf(x[c], a.scale_log2, -mu));
-            const float p1 = fast_exp2(fmaf(x[c + 1], a.scale_log2, -mu));
-            rs8[c & 7] += p0;
-            rs8[(c + 1) & 7] += p1;
-            pk[c >> 1] = __uint_as_float(MmaOp<T>::pack(p0, p1));
+            for (int c = 0; c < 16; c += 2) {
+              const float p0 = fast_exp2(fmaf(x[16 * h + c], a.scale_log2, -mu));
+              const float p1 = fast_exp2(fmaf(x[16 * h + c + 1], a.scale_log2, -mu));
+              rs8[c & 7] += p0;
+              rs8[(c + 1) & 7] += p1;
+              pk[c >> 1] = __uint_as_float(MmaOp<T>::pack(p0, p1));
+            }
+            tc05::st_32x32b_x8(s_self + 64 + group * 16 + h * 8, pk);
           }
-          tc05::st_32x32b_x16(s_self + c32 * 16, pk);
-        }
+        };
+        exp_chunk(va, 0);                           // keys 64..95  -> columns 64..79
+        exp_chunk(vb, 1);                           // keys 96..127 -> columns 80..95
+        tc05::ld_32x32b_x32(s_self, va);            // keys 0..63 again (one wait)
+        tc05::ld_32x32b_x32(s_self + 32, vb);
+        tc05::wait_ld();
+        mask_chunk(va, 0);
+        mask_chunk(vb, 1);
+        exp_chunk(va, 2);                           // keys 0..31   -> columns 96..111
+        exp_chunk(vb, 3);                           // keys 32..63  -> columns 112..127
         const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
                          ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         l = l * alpha + rs;
