@@ -95,7 +95,7 @@ struct RowArgs {
   int32_t* status;
 };
 
-constexpr int kPrefillThreads = 352;
+constexpr int kPrefillThreads = 384;
 
 struct PrefillHeader {
   int32_t total_items;

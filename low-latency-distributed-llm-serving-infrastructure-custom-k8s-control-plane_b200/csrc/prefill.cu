@@ -4,23 +4,26 @@
 // tile are the G query heads sharing the KV head x TQ tokens (row = g*TQ + t), so every K/V tile
 // fetched from HBM feeds all G heads.  K/V are read through the block table in 128-key tiles.
 //
-// Warp roles (352 threads):
-//   warp 0      TMA producer for Q (4-D map over [token][head][dim]) and K tiles (3-D map over the
-//               paged cache, one 16-row box per block and 64-column half), kKStages-deep ring.
-//   warp 10     TMA producer for V tiles, kVStages-deep ring.  K and V are issued by different
-//               threads: a block-paged tile is 8*D/64 small boxes, and one thread issuing both
-//               rings could not keep the tensor core fed.
-//   warp 1      TMEM owner and MMA issuer (one thread).  S = Q.K^T (M=128, N=128, K=D) into the
-//               TMEM S buffer of the warpgroup that owns the tile; O += P.V (M=128, N=D, K=128)
-//               with P read straight from TMEM (the A operand of tcgen05.mma in tensor memory)
-//               into that warpgroup's O accumulator; tcgen05.commit on mbarriers.
-//   warps 2-5,  two softmax warpgroups.  Warpgroup w takes the KV tiles g with g % 2 == w and keeps
-//   warps 6-9   its own running max / sum and its own O accumulator, so the two run concurrently
+// Warp roles (384 threads, three warpgroups of one kind each so that registers can be moved
+// between them with setmaxnreg: the softmax warpgroups get kRegsSoftmax per thread, the
+// producer / MMA warpgroup kRegsOther):
+//   warps 0-3,  two softmax warpgroups.  Warpgroup w takes the KV tiles g with g % 2 == w and keeps
+//   warps 4-7   its own running max / sum and its own O accumulator, so the two run concurrently
 //               without exchanging anything per tile.  One query row per thread (TMEM lane = row):
 //               tcgen05.ld of S, causal mask, online softmax in fp32, P packed to bf16/f16 pairs
 //               and stored with tcgen05.st over the S columns already consumed, rescale of O in
 //               TMEM when the row max moves.  The epilogue merges the two partial (O, max, sum)
 //               triples of each row, as a two-way split-KV combine, and writes O / l.
+//   warp 8      TMA producer for Q (4-D map over [token][head][dim]) and K tiles (3-D map over the
+//               paged cache, one 16-row box per block and 64-column half), kKStages-deep ring.
+//   warp 10     TMA producer for V tiles, kVStages-deep ring.  K and V are issued by different
+//               threads: a block-paged tile is 8*D/64 small boxes, and one thread issuing both
+//               rings could not keep the tensor core fed.
+//   warp 9      TMEM owner and MMA issuer (one thread).  S = Q.K^T (M=128, N=128, K=D) into the
+//               TMEM S buffer of the warpgroup that owns the tile; O += P.V (M=128, N=D, K=128)
+//               with P read straight from TMEM (the A operand of tcgen05.mma in tensor memory)
+//               into that warpgroup's O accumulator; tcgen05.commit on mbarriers.
+//   warp 11     idle (completes the third warpgroup).
 // TMEM (512 columns): S/P of warpgroup w at columns [128w, 128w+128) (P in the upper 64), O of
 // warpgroup w at [256 + w*D, 256 + (w+1)*D).  P(g) aliases S(g); S(g+2) is issued right after
 // PV(g) (in-order tcgen05.mma execution orders PV(g)'s TMEM reads before S(g+2)'s writes).
@@ -43,6 +46,13 @@ __device__ constexpr uint32_t kPChunk[4] = {2, 3, 0, 1};
 constexpr int kKStages = 3;
 constexpr int kVStages = 2;
 constexpr int kSoftmaxWarps = 8;
+// Register split (setmaxnreg): 256 softmax threads x kRegsSoftmax + 128 other threads x
+// kRegsOther must not exceed the 384 x (registers per thread at launch) the CTA is given; the
+// launcher checks the compiled count before every first launch (a larger request would wait
+// forever).
+constexpr uint32_t kRegsSoftmax = 176;
+constexpr uint32_t kRegsOther = 136;
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;
 
 struct SmemLayout {
   uint32_t q, k0, v0, bars, xch, total;
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     *abort_flag = 0;
     fence_proxy_async_smem();
   }
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tc05::tmem_alloc(tmem_slot, kTmemCols);
     tc05::tmem_relinquish();
   }
@@ -201,6 +211,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   tc05::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const int total = a.hdr->total_items;
+  // move registers from the producer / MMA warpgroup to the two softmax warpgroups
+  if (warp >= 8)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
+  else
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
 
   auto decode_item = [&](int item, int& s, int& h, int& q_row0, int& n_q, int& pos0, int& kv_end,
                          int& ctx) {
@@ -218,12 +233,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     kv_end = pos0 + n_q;
   };
 
-  if (warp == 0 || warp == 10) {
+  if (warp == kWarpK || warp == kWarpV) {
     // ------------------------------------------------------------------ TMA producers
     // The whole warp runs the loop (warp-uniform coordinates); the elected lane issues.
     {
       const bool leader = elect_one_sync();
-      const bool is_k = warp == 0;
+      const bool is_k = warp == kWarpK;
       const CUtensorMap* map = is_k ? &kmap : &vmap;
       const uint32_t nst = is_k ? kKStages : kVStages;
       uint64_t* full = &bars[is_k ? kBarKFull : kBarVFull];
@@ -309,7 +324,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       if (q_issued > 0) mbar_wait_bounded(&bars[kBarQFull], (q_issued - 1) & 1u);
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop and waits (warp-uniform descriptors); the elected lane issues
     // the MMAs and commits.
@@ -414,10 +429,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       mbar_wait_bounded(&bars[kBarFinal], 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------------ softmax / epilogue
-    // warps 2-5 = warpgroup 0, warps 6-9 = warpgroup 1; TMEM lane quarter = warp % 4
-    const uint32_t wg = static_cast<uint32_t>(warp - 2) >> 2;
+    // warps 0-3 = warpgroup 0, warps 4-7 = warpgroup 1; TMEM lane quarter = warp % 4
+    const uint32_t wg = static_cast<uint32_t>(warp) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int g = row / a.tq;
@@ -425,7 +440,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t s_self = trow + wg * kBN;
     const uint32_t o_self = trow + kColO + wg * D;
-    const int sm_tid = (warp - 2 - 4 * static_cast<int>(wg)) * 32 + lane;  // 0..127
+    const int sm_tid = (warp & 3) * 32 + lane;  // 0..127 within the warpgroup
     float2* xch = reinterpret_cast<float2*>(smem + L.xch);
     uint32_t s_it = 0, kv_it = 0, n_items = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
@@ -647,7 +662,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 
   tc05::fence_before_sync();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tc05::fence_after_sync();
     tc05::tmem_dealloc(tmem, kTmemCols);
   }
@@ -664,7 +679,16 @@ static cudaError_t launch_prefill_tc_t(const CUtensorMap& qm, const CUtensorMap&
   static bool configured = false;
   auto kern = prefill_tc_kernel<T, D>;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // the register split must fit the registers the CTA is launched with
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (static_cast<long>(fa.numRegs) * kPrefillThreads <
+        256L * kRegsSoftmax + 128L * kRegsOther) {
+      set_last_error("prefill kernel compiled with too few registers for its register split");
+      return cudaErrorInvalidConfiguration;
+    }
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
