@@ -3,7 +3,7 @@
 Run in a container that has the reference tree and its compiled binding:
 
     make -C oracle ref
-    PYTHONPATH=/root/reference:oracle/_ref python tests/golden/make_golden.py
+    PYTHONPATH=<reference checkout>:oracle/_ref python tests/golden/make_golden.py
 
 It imports the reference's own Python (app.memory.manager.PagedKVCacheManager,
 app.model.paged_attention.PagedStepContext, app.scheduler.Scheduler, app.engine.LLMEngine with
