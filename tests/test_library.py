@@ -38,3 +38,37 @@ def test_status_strings(pkg):
     L = _native.lib()
     assert L.b200_status_string(0) == b"ok"
     assert L.b200_status_string(2) == b"out of memory"
+
+
+def _decode_workspace_layout(S, max_ctx, split, hkv=8, G=4, D=128):
+    """The decode workspace layout (header, split offsets, work list, merge counters, partial
+    lse and o) for a given split length, restated from the library's plan."""
+    a256 = lambda x: (x + 255) & ~255
+    ips = hkv * ((G + 7) // 8)
+    hpc = min(G, 8)
+    ms = S * ((max_ctx + split - 1) // split)
+    return (a256(16) + a256((S + 1) * 4) + a256(ms * 8) + a256(S * ips * 4) + a256(ms * ips * hpc * 4)
+            + a256(ms * ips * hpc * D * 4))
+
+
+def test_decode_split_rule_on_host(pkg):
+    """Pins the split rule through the workspace size (host arithmetic, no GPU needed; without a
+    device the library plans for 148 SMs): the longest power-of-two split from 4096 down to 64
+    that leaves at least 8 (sequence, split, kv head) items per resident CTA (2 per SM)."""
+    from llm_serving_b200 import _native as N
+    L = N.lib()
+
+    def ws(S, max_ctx):
+        p = N.DecodeParams()
+        p.geom = N.CacheGeometry(1, 1024, 16, 8, 128, N.DTYPE_BF16)
+        p.num_query_heads, p.num_seqs, p.max_context_len = 32, S, max_ctx
+        p.q_stride_row, p.q_stride_head = 32 * 128, 128
+        return int(L.b200_paged_decode_workspace_bytes(ctypes.byref(p)))
+
+    # config 2: 256 sequences, contexts up to 4096 -> 2048-token splits
+    assert ws(256, 4096) == _decode_workspace_layout(256, 4096, 2048)
+    assert ws(256, 4096) != _decode_workspace_layout(256, 4096, 4096)
+    # a long-context batch of 14 sequences -> 1024
+    assert ws(14, 33792) == _decode_workspace_layout(14, 33792, 1024)
+    # a tiny batch bottoms out at 64
+    assert ws(4, 700) == _decode_workspace_layout(4, 700, 64)
