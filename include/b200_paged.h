@@ -261,7 +261,25 @@ int b200_pool_destroy(B200BlockPool* pool);
 int b200_pool_append_tokens(B200BlockPool* pool, int32_t slot, int32_t n);
 /* Queue: free the slot's blocks in table order and reset it (release_internal, :461-469). */
 int b200_pool_release(B200BlockPool* pool, int32_t slot);
-/* Apply the queued ops on `stream` (one small H2D copy + one kernel).  No host sync. */
+/* Prefix sharing.  The empty slot dst_slot takes the first num_blocks blocks of src_slot, each
+ * gaining an owner (PageAllocator::share_block + SequenceBlockTable::append_block,
+ * page_allocator.hpp:142-149, :409-413); dst_slot then counts num_blocks * block_size tokens.
+ * A shared block returns to the free list only when its last owner releases it.  Flushes of
+ * batches that involve shared blocks apply their ops in order on one thread and read the exact
+ * free count back (one stream synchronisation). */
+int b200_pool_share(B200BlockPool* pool, int32_t dst_slot, int32_t src_slot, int32_t num_blocks);
+/* Copy-on-write: table entry block_index of the slot gets a fresh block from the front of the free
+ * list and the old block loses an owner (allocate_block + SequenceBlockTable::replace_block +
+ * free_block, page_allocator.hpp:100-127, :416-424, :151-177).  After the flush,
+ * b200_pool_cow_pairs gives the (old, new) block ids of every replacement of that flush as two
+ * device arrays, ready for b200_copy_blocks (so the copy needs no host round trip).  Replace only
+ * blocks that have another owner: a sole owner's old block would be freed in the same flush. */
+int b200_pool_copy_on_write(B200BlockPool* pool, int32_t slot, int32_t block_index);
+int32_t b200_pool_cow_pairs(const B200BlockPool* pool, const int32_t** old_blocks,
+                            const int32_t** new_blocks);
+
+/* Apply the queued ops on `stream` (one small H2D copy + one kernel).  No host sync, except for
+ * batches that involve shared blocks (see b200_pool_share). */
 int b200_pool_flush(B200BlockPool* pool, void* stream);
 /* Host-side counts (exact; no device access). */
 int32_t b200_pool_num_free_blocks(const B200BlockPool* pool);

@@ -100,6 +100,9 @@ SIGNATURES = [
     ("b200_pool_destroy", ctypes.c_int, [c_vp]),
     ("b200_pool_append_tokens", ctypes.c_int, [c_vp, c_i32, c_i32]),
     ("b200_pool_release", ctypes.c_int, [c_vp, c_i32]),
+    ("b200_pool_share", ctypes.c_int, [c_vp, c_i32, c_i32, c_i32]),
+    ("b200_pool_copy_on_write", ctypes.c_int, [c_vp, c_i32, c_i32]),
+    ("b200_pool_cow_pairs", c_i32, [c_vp, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp)]),
     ("b200_pool_flush", ctypes.c_int, [c_vp, c_vp]),
     ("b200_pool_num_free_blocks", c_i32, [c_vp]),
     ("b200_pool_tokens", c_i32, [c_vp, c_i32]),

@@ -70,6 +70,27 @@ class DeviceBlockPool:
     def release(self, slot: int) -> None:
         N.check(N.lib().b200_pool_release(self._h, int(slot)))
 
+    def share(self, dst_slot: int, src_slot: int, num_blocks: int) -> None:
+        """The empty ``dst_slot`` takes the first ``num_blocks`` blocks of ``src_slot`` (each
+        gains an owner; it returns to the free list with its last owner's release)."""
+        N.check(N.lib().b200_pool_share(self._h, int(dst_slot), int(src_slot), int(num_blocks)))
+
+    def copy_on_write(self, slot: int, block_index: int) -> None:
+        """Queue: table entry ``block_index`` of ``slot`` gets a fresh block (the old one loses an
+        owner).  After the flush, ``cow_pairs()`` gives the (old, new) ids to copy."""
+        N.check(N.lib().b200_pool_copy_on_write(self._h, int(slot), int(block_index)))
+
+    def cow_pairs(self):
+        """(old, new) block ids of the last flush's copy-on-write replacements, as int32 device
+        views (empty when there were none)."""
+        old, new = ctypes.c_void_p(), ctypes.c_void_p()
+        n = int(N.lib().b200_pool_cow_pairs(self._h, ctypes.byref(old), ctypes.byref(new)))
+        if n == 0:
+            e = torch.empty(0, dtype=torch.int32, device=self.device)
+            return e, e
+        mk = lambda ptr: torch.as_tensor(_DeviceArray(ptr.value, (n,), "<i4"), device=self.device)
+        return mk(old), mk(new)
+
     def flush(self, stream: Optional[int] = None) -> None:
         with torch.cuda.device(self.device):
             N.check(N.lib().b200_pool_flush(self._h, _stream(self.device) if stream is None

@@ -7,7 +7,8 @@
 // freed counts), then allocations (each ALLOC takes ring[head + exclusive prefix of the allocated
 // counts]).  Because the host only queues an ALLOC when its running free count covers it, every
 // ring position an ALLOC reads was written by a RELEASE that precedes it in queue order, so the
-// two-phase kernel hands out exactly the blocks the reference's sequential loop would.
+// two-phase kernel hands out exactly the blocks the reference's sequential loop would.  Batches
+// that involve shared blocks go through an ordered one-thread kernel instead.
 //
 // The metadata kernels build what PagedStepContext (app/model/paged_attention.py:40-90) and
 // build_block_tables (app/memory/manager.py:236-271) build on the host: cu_seqlens, cu_context,
@@ -108,6 +109,81 @@ __global__ void __launch_bounds__(1024) pool_apply_kernel(PoolApplyArgs a) {
   }
 }
 
+// Ordered apply, for batches with shared blocks (SHARE / REPLACE ops, or releases of sequences that
+// hold shared blocks): a block goes back to the free list only when its last owner lets it go
+// (PageAllocator::free_block, page_allocator.hpp:151-177), so where freed blocks land depends on
+// every earlier op; one thread applies the batch in queue order, exactly as the reference's
+// sequential calls would (share_block :142-149, replace_block :416-424, allocate_block
+// :100-127).  Sharing is rare; the parallel kernel above serves everything else.
+__global__ void pool_apply_ordered_kernel(PoolApplyArgs a, int32_t* cow_src, int32_t* cow_dst) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  int64_t head = a.head_tail[0];
+  int64_t tail = a.head_tail[1];
+  int32_t k = 0;
+  auto valid = [&](int32_t b) { return b >= 0 && b < a.nb; };
+  auto release_one = [&](int32_t b) {
+    if (!valid(b) || a.refcount[b] <= 0) {
+      flag_status(a.status, B200_DEVICE_BAD_OP);
+      return;
+    }
+    if (--a.refcount[b] == 0) a.ring[(tail++) % a.nb] = b;
+  };
+  for (int i = 0; i < a.num_ops; ++i) {
+    const PoolOp op = a.ops[i];
+    int32_t* row = a.tables + static_cast<int64_t>(op.slot) * a.table_stride;
+    if (op.kind == 0) {
+      for (int32_t j = 0; j < op.count; ++j) {
+        if (head >= tail || op.first + j >= a.table_stride) {
+          flag_status(a.status, B200_DEVICE_BAD_OP);
+          break;
+        }
+        const int32_t b = a.ring[(head++) % a.nb];
+        a.refcount[b] = 1;
+        row[op.first + j] = b;
+      }
+      if (a.nblocks[op.slot] < op.first + op.count) a.nblocks[op.slot] = op.first + op.count;
+    } else if (op.kind == 1) {
+      for (int32_t j = 0; j < op.count; ++j) {
+        release_one(row[j]);
+        row[j] = -1;
+      }
+      a.nblocks[op.slot] = 0;
+    } else if (op.kind == 2) {
+      const int32_t* src = a.tables + static_cast<int64_t>(op.first) * a.table_stride;
+      for (int32_t j = 0; j < op.count; ++j) {
+        const int32_t b = src[j];
+        if (!valid(b) || a.refcount[b] <= 0) {
+          flag_status(a.status, B200_DEVICE_BAD_OP);
+          row[j] = -1;
+          continue;
+        }
+        ++a.refcount[b];
+        row[j] = b;
+      }
+      a.nblocks[op.slot] = op.count;
+    } else if (op.kind == 3) {
+      const int32_t old = row[op.first];
+      if (head >= tail || !valid(old)) {
+        flag_status(a.status, B200_DEVICE_BAD_OP);
+        cow_src[k] = cow_dst[k] = -1;  // the copy kernel skips (and flags) this pair
+        ++k;
+        continue;
+      }
+      const int32_t b = a.ring[(head++) % a.nb];
+      a.refcount[b] = 1;
+      row[op.first] = b;
+      release_one(old);
+      cow_src[k] = old;
+      cow_dst[k] = b;
+      ++k;
+    } else {
+      flag_status(a.status, B200_DEVICE_BAD_OP);
+    }
+  }
+  a.head_tail[0] = head;
+  a.head_tail[1] = tail;
+}
+
 // K4 part 1: scans (one CTA).
 __global__ void __launch_bounds__(1024) meta_scan_kernel(MetaArgs a) {
   __shared__ int64_t warp_buf[32];
@@ -186,6 +262,13 @@ cudaError_t launch_pool_init(int32_t* ring, int32_t* refcount, int32_t* tables, 
 cudaError_t launch_pool_apply(const PoolApplyArgs& a, cudaStream_t stream) {
   if (a.num_ops <= 0) return cudaSuccess;
   pool_apply_kernel<<<1, 1024, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool_apply_ordered(const PoolApplyArgs& a, int32_t* cow_src, int32_t* cow_dst,
+                                      cudaStream_t stream) {
+  if (a.num_ops <= 0) return cudaSuccess;
+  pool_apply_ordered_kernel<<<1, 32, 0, stream>>>(a, cow_src, cow_dst);
   return cudaGetLastError();
 }
 

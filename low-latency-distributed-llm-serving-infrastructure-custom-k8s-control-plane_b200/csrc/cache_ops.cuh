@@ -60,6 +60,10 @@ cudaError_t launch_copy_blocks(const BlockCopyArgs& a, int vec_bytes, int num_sm
 // One queued block-pool op, uploaded as 4 int32.
 //   kind 0 = ALLOC:   append `count` blocks to slot's table starting at table index `first`
 //   kind 1 = RELEASE: free the slot's first `count` blocks in table order, clear the row
+//   kind 2 = SHARE:   the (empty) slot takes the first `count` blocks of slot `first`, each
+//                     block's owner count + 1
+//   kind 3 = REPLACE: table entry `first` of the slot gets a fresh block (copy-on-write); the old
+//                     block loses an owner and is freed if that was the last one
 struct PoolOp {
   int32_t kind, slot, first, count;
 };
@@ -78,6 +82,10 @@ struct PoolApplyArgs {
 };
 
 cudaError_t launch_pool_apply(const PoolApplyArgs& a, cudaStream_t stream);
+// All four kinds, strictly in queue order (one thread); REPLACE k records its (old, new) block
+// pair in cow_src[k] / cow_dst[k].
+cudaError_t launch_pool_apply_ordered(const PoolApplyArgs& a, int32_t* cow_src, int32_t* cow_dst,
+                                      cudaStream_t stream);
 cudaError_t launch_pool_init(int32_t* ring, int32_t* refcount, int32_t* tables, int32_t* nblocks,
                              int64_t* head_tail, int32_t nb, int64_t table_elems, int32_t max_seqs,
                              cudaStream_t stream);

@@ -31,7 +31,13 @@ struct B200BlockPool {
   bool initialised = false;
   int64_t free_count = 0;
   std::vector<int32_t> tokens, nblocks;
+  std::vector<uint8_t> shared;    // slot holds (or held out) blocks with more than one owner
   std::vector<b200::PoolOp> queue;
+  bool ordered = false;           // queue holds SHARE / REPLACE or a release of a shared slot
+  int32_t pending_replace = 0;    // REPLACE ops in the queue
+  int32_t* d_cow = nullptr;       // [cow_cap] old blocks, then [cow_cap] new blocks
+  int32_t cow_cap = 0;
+  int32_t cow_count = 0;          // pairs recorded by the last flush
 };
 
 namespace {
@@ -73,6 +79,47 @@ int flush_segment(B200BlockPool* p, const b200::PoolOp* ops, int32_t n, cudaStre
   return B200_OK;
 }
 
+// Ordered path: the whole queue by the one-thread kernel, then the exact free count read back
+// (a shared block is freed only with its last owner, which the host cannot see).
+int flush_ordered(B200BlockPool* p, cudaStream_t st) {
+  const int32_t n = static_cast<int32_t>(p->queue.size());
+  int rc = ensure_ops_capacity(p, n);
+  if (rc != B200_OK) return rc;
+  if (p->pending_replace > p->cow_cap) {
+    int32_t cap = p->cow_cap > 0 ? p->cow_cap : 64;
+    while (cap < p->pending_replace) cap *= 2;
+    if (p->d_cow) cudaFree(p->d_cow);
+    p->d_cow = nullptr;
+    p->cow_cap = 0;
+    if (cudaMalloc(&p->d_cow, 2 * static_cast<size_t>(cap) * sizeof(int32_t)) != cudaSuccess)
+      return pfail(B200_ERR_CUDA, "copy-on-write pair buffer allocation failed");
+    p->cow_cap = cap;
+  }
+  if (cudaMemcpyAsync(p->d_ops, p->queue.data(), n * sizeof(b200::PoolOp),
+                      cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return pfail(B200_ERR_CUDA, "pool op upload failed");
+  b200::PoolApplyArgs a{};
+  a.ops = p->d_ops;
+  a.num_ops = n;
+  a.nb = p->total_blocks;
+  a.table_stride = p->max_blocks;
+  a.ring = p->d_ring;
+  a.tables = p->d_tables;
+  a.nblocks = p->d_nblocks;
+  a.refcount = p->d_refcount;
+  a.head_tail = p->d_head_tail;
+  a.status = p->d_status;
+  if (b200::launch_pool_apply_ordered(a, p->d_cow, p->d_cow + p->cow_cap, st) != cudaSuccess)
+    return pfail(B200_ERR_CUDA, "pool apply launch failed");
+  int64_t ht[2];
+  if (cudaMemcpyAsync(ht, p->d_head_tail, sizeof(ht), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return pfail(B200_ERR_CUDA, "pool free-count read-back failed");
+  p->free_count = ht[1] - ht[0];
+  p->cow_count = p->pending_replace;
+  return B200_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -92,6 +139,7 @@ int b200_pool_create(int32_t total_blocks, int32_t block_size, int32_t max_seqs,
   p->free_count = total_blocks;
   p->tokens.assign(max_seqs, 0);
   p->nblocks.assign(max_seqs, 0);
+  p->shared.assign(max_seqs, 0);
   const int64_t table_elems = static_cast<int64_t>(max_seqs) * max_blocks_per_seq;
   bool ok = cudaMalloc(&p->d_ring, total_blocks * sizeof(int32_t)) == cudaSuccess &&
             cudaMalloc(&p->d_refcount, total_blocks * sizeof(int32_t)) == cudaSuccess &&
@@ -123,6 +171,7 @@ int b200_pool_destroy(B200BlockPool* p) {
   cudaFree(p->d_head_tail);
   cudaFree(p->d_status);
   if (p->d_ops) cudaFree(p->d_ops);
+  if (p->d_cow) cudaFree(p->d_cow);
   delete p;
   return B200_OK;
 }
@@ -161,17 +210,70 @@ int b200_pool_release(B200BlockPool* p, int32_t slot) {
   if (slot < 0 || slot >= p->max_seqs) return pfail(B200_ERR_OUT_OF_RANGE, "sequence slot out of range");
   const int32_t nb = p->nblocks[slot];
   if (nb > 0) p->queue.push_back(b200::PoolOp{1, slot, 0, nb});
-  p->free_count += nb;
+  if (p->shared[slot]) {
+    // some of these blocks have other owners: how many come free is known after the flush
+    if (nb > 0) p->ordered = true;
+    p->shared[slot] = 0;
+  } else {
+    p->free_count += nb;
+  }
   p->tokens[slot] = 0;
   p->nblocks[slot] = 0;
   return B200_OK;
 }
 
+int b200_pool_share(B200BlockPool* p, int32_t dst_slot, int32_t src_slot, int32_t num_blocks) {
+  if (p == nullptr) return pfail(B200_ERR_INVALID_ARGUMENT, "null pool");
+  if (dst_slot < 0 || dst_slot >= p->max_seqs || src_slot < 0 || src_slot >= p->max_seqs)
+    return pfail(B200_ERR_OUT_OF_RANGE, "sequence slot out of range");
+  if (dst_slot == src_slot) return pfail(B200_ERR_INVALID_ARGUMENT, "a slot cannot share with itself");
+  if (p->nblocks[dst_slot] != 0)
+    return pfail(B200_ERR_INVALID_ARGUMENT, "the receiving slot must be empty");
+  if (num_blocks <= 0 || num_blocks > p->nblocks[src_slot])
+    return pfail(B200_ERR_INVALID_ARGUMENT, "num_blocks must be in [1, blocks of the source slot]");
+  p->queue.push_back(b200::PoolOp{2, dst_slot, src_slot, num_blocks});
+  p->nblocks[dst_slot] = num_blocks;
+  p->tokens[dst_slot] = num_blocks * p->block_size;
+  p->shared[dst_slot] = p->shared[src_slot] = 1;
+  p->ordered = true;
+  return B200_OK;
+}
+
+int b200_pool_copy_on_write(B200BlockPool* p, int32_t slot, int32_t block_index) {
+  if (p == nullptr) return pfail(B200_ERR_INVALID_ARGUMENT, "null pool");
+  if (slot < 0 || slot >= p->max_seqs) return pfail(B200_ERR_OUT_OF_RANGE, "sequence slot out of range");
+  if (block_index < 0 || block_index >= p->nblocks[slot])
+    return pfail(B200_ERR_OUT_OF_RANGE, "block index out of range");
+  if (p->free_count < 1)
+    return pfail(B200_ERR_OUT_OF_MEMORY, "Out of Memory: No free VRAM pages available in KV-Cache pool!");
+  p->queue.push_back(b200::PoolOp{3, slot, block_index, 1});
+  p->free_count -= 1;
+  ++p->pending_replace;
+  p->ordered = true;
+  return B200_OK;
+}
+
+int32_t b200_pool_cow_pairs(const B200BlockPool* p, const int32_t** old_blocks,
+                            const int32_t** new_blocks) {
+  if (p == nullptr) return 0;
+  if (old_blocks) *old_blocks = p->d_cow;
+  if (new_blocks) *new_blocks = p->d_cow ? p->d_cow + p->cow_cap : nullptr;
+  return p->cow_count;
+}
+
 int b200_pool_flush(B200BlockPool* p, void* stream) {
   if (p == nullptr) return pfail(B200_ERR_INVALID_ARGUMENT, "null pool");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  p->cow_count = 0;
+  if (p->ordered) {
+    const int rc = p->queue.empty() ? B200_OK : flush_ordered(p, st);
+    p->queue.clear();
+    p->ordered = false;
+    p->pending_replace = 0;
+    return rc;
+  }
   // The apply kernel runs all RELEASEs of a launch before its ALLOCs, so a RELEASE of a slot that
   // an earlier ALLOC of the same launch filled starts a new launch.
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   std::vector<uint8_t> allocated(p->max_seqs, 0);
   size_t seg = 0;
   int rc = B200_OK;

@@ -231,6 +231,26 @@ class PagedKVCacheManager:
         slot_mapping = self.build_slot_mapping([seq], [token_index], [1])
         self.scatter_kv(key_token.unsqueeze(0), value_token.unsqueeze(0), slot_mapping)
 
+    # ---- prefix sharing (page_allocator.hpp:142-149, :409-424) --------------------------------
+    def share_prefix(self, src_seq, dst_seq, num_blocks: int) -> None:
+        """``dst_seq`` (no blocks yet) starts with the first ``num_blocks`` blocks of ``src_seq``
+        (shared, not copied): its table holds them and it counts num_blocks * block_size
+        tokens.  Before either sequence writes into a shared block, call ``copy_on_write``."""
+        self.init_sequence_table(dst_seq)
+        self.pool.share(dst_seq.block_table.slot, src_seq.block_table.slot, num_blocks)
+
+    def copy_on_write(self, seq, block_indices) -> None:
+        """Give ``seq`` private copies of its shared blocks at the given table indices: fresh
+        blocks replace them in its table (flushed now) and the K/V of every layer is copied from
+        the old blocks on the device, with no host round trip for the block ids."""
+        for i in block_indices:
+            self.pool.copy_on_write(seq.block_table.slot, int(i))
+        self.pool.flush()
+        old, new = self.pool.cow_pairs()
+        if old.numel():
+            paged_ops.copy_blocks(self.key_cache, self.value_cache, self.key_cache,
+                                  self.value_cache, old, new, device=self._device)
+
     # ---- block copies (strategies.py:117-122) -------------------------------------------------
     def copy_blocks(self, src_blocks, dst_blocks) -> None:
         """Copy device blocks ``src_blocks[i] -> dst_blocks[i]`` (every layer, K and V) -- the
