@@ -272,8 +272,8 @@ class HostSwapSpace:
         L, _, BS, H, D = manager.key_cache.shape
         shape = (L, int(num_blocks), BS, H, D)
         self.manager = manager
-        self.key_cache = torch.empty(shape, dtype=manager.dtype).pin_memory()
-        self.value_cache = torch.empty(shape, dtype=manager.dtype).pin_memory()
+        self.key_cache = torch.empty(shape, dtype=manager.dtype, pin_memory=True)
+        self.value_cache = torch.empty(shape, dtype=manager.dtype, pin_memory=True)
 
     def swap_out(self, device_blocks, host_blocks) -> None:
         """Device block ``device_blocks[i]`` -> host block ``host_blocks[i]``."""
