@@ -713,8 +713,8 @@ def swap_arm(args):
     shape = (Ln, nb_dev, 16, 8, 128)
     kc = torch.randn(shape, device=dev).to(torch.bfloat16)
     vc = torch.randn(shape, device=dev).to(torch.bfloat16)
-    hk = torch.empty((Ln, nb_host, 16, 8, 128), dtype=torch.bfloat16).pin_memory()
-    hv = torch.empty_like(hk).pin_memory()
+    hk = torch.empty((Ln, nb_host, 16, 8, 128), dtype=torch.bfloat16, pin_memory=True)
+    hv = torch.empty_like(hk, pin_memory=True)
     g = torch.Generator().manual_seed(9)
     perm = torch.randperm(nb_dev, generator=g).to(torch.int32)
     dev_ids, dev_ids2 = perm[:n].to(dev), perm[n:2 * n].to(dev)  # disjoint: no block is both
@@ -741,7 +741,7 @@ def swap_arm(args):
     # round trip: the swapped-in (and then device-copied) blocks equal the swapped-out ones
     ok = bool(torch.equal(kc[:, dev_ids2.long()].cpu(), hk[:, host_ids.long().cpu()]))
     big_d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
-    big_h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    big_h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
     ms_d2h = timed(lambda: big_h.copy_(big_d, non_blocking=True))
     ms_h2d = timed(lambda: big_d.copy_(big_h, non_blocking=True))
     hbm, src = load_peaks()
