@@ -282,8 +282,8 @@ def ours_arm(args):
 
     # e2e through the public API with host buffers: every step copies its inputs from pinned host
     # memory and reads its result back, inside the timed region.  As a serving loop would, the
-    # copies run on a copy stream with two buffer sets: step i+1's inputs go up while step i
-    # decodes, and step i's output comes back while step i+1 computes.
+    # copies run on one stream per direction with two buffer sets: step i+1's inputs go up while
+    # step i decodes, and step i's output comes back while step i+1 computes.
     h_in = {"q": q.cpu().pin_memory(), "k": newk.cpu().pin_memory(),
             "v": newv.cpu().pin_memory(), "slots": slots.cpu().pin_memory(),
             "bt": bt.cpu().pin_memory(), "ctx": ctx.cpu().pin_memory()}
@@ -293,31 +293,35 @@ def ours_arm(args):
         bset["out"] = torch.empty_like(out)
     h2d = sum(t.numel() * t.element_size() for t in h_in.values())
     d2h = h_out[0].numel() * h_out[0].element_size()
-    copy = torch.cuda.Stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)  # one copy engine per direction
     ready = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
+    fetched = [torch.cuda.Event() for _ in range(2)]
 
     def upload(i):
         bset = bufs[i % 2]
-        with torch.cuda.stream(copy):
+        with torch.cuda.stream(up):
             if i >= 2:
-                copy.wait_event(done[i % 2])  # step i-2 has finished with this buffer set
+                up.wait_event(done[i % 2])  # step i-2 has finished reading this buffer set
             for n, t in h_in.items():
                 bset[n].copy_(t, non_blocking=True)
-            ready[i % 2].record(copy)
+            ready[i % 2].record(up)
 
     def compute(i):
         bset = bufs[i % 2]
         stream.wait_event(ready[i % 2])
+        if i >= 2:
+            stream.wait_event(fetched[i % 2])  # step i-2's output has been read back
         paged_ops.reshape_and_cache(bset["k"], bset["v"], kc, vc, bset["slots"], 0)
         paged_ops.paged_decode(bset["q"], kc, vc, 0, bset["bt"], bset["ctx"], b.scale, max_ctx,
                                out=bset["out"])
         done[i % 2].record(stream)
 
     def download(i):
-        with torch.cuda.stream(copy):
-            copy.wait_event(done[i % 2])
+        with torch.cuda.stream(down):
+            down.wait_event(done[i % 2])
             h_out[i % 2].copy_(bufs[i % 2]["out"], non_blocking=True)
+            fetched[i % 2].record(down)
 
     def e2e_run(n):
         upload(0)
@@ -326,7 +330,8 @@ def ours_arm(args):
                 upload(i + 1)
             compute(i)
             download(i)
-        stream.wait_stream(copy)
+        stream.wait_stream(up)
+        stream.wait_stream(down)
 
     e2e_run(3)
     torch.cuda.synchronize(dev)
@@ -335,7 +340,8 @@ def ours_arm(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    copy.wait_stream(stream)
+    up.wait_stream(stream)
+    down.wait_stream(stream)
     e2e_run(args.steps)
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -386,8 +392,8 @@ def ours_arm(args):
                                % decode_bytes},
         "e2e": {"value": round(world * total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9, 2),
                 "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "pipelining": "copy stream, two buffer sets: inputs of step i+1 and output of "
-                              "step i-1 move while step i computes",
+                "pipelining": "one copy stream per direction, two buffer sets: inputs of step "
+                              "i+1 and output of step i-1 move while step i computes",
                 "output_matches_device_run": e2e_ok},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
