@@ -169,6 +169,61 @@ def run_cpu_kernel(b, seqs, repeats=1, min_seconds=0.0):
     return nbytes * passes / dt / 1e9, dt / passes, kind, cores, passes
 
 
+def cpu_mixed_sample(b, num_prefill, rows_per_chunk=256, num_decode=16, seed=2):
+    """Reference-kernel calls for a bounded sample of a mixed ragged step (config 3), shaped the
+    way the reference would be driven: one call per prefill chunk with a causal mask over the
+    chunk's whole context (prior tokens + the chunk), one call per decode sequence.  Each chunk
+    call keeps only the chunk's first `rows_per_chunk` query rows; the reference computes every
+    row against the full context whatever the mask (paged_kernels.cpp:27-104), so a row costs
+    the same as in the whole chunk.  Returns [(q, kc, vc, gs, mask, rows, causal_flops)]."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    Hq, Hkv, D, BS = b.num_query_heads, b.num_kv_heads, b.head_dim, b.block_size
+
+    def bf16(shape):
+        x = rng.standard_normal(shape, dtype=np.float32)
+        return O.bf16_bits_to_f32(O.f32_to_bf16_bits(x)).reshape(shape)
+
+    calls = []
+    picks = list(range(num_prefill)) + list(range(num_prefill, min(b.num_seqs, num_prefill + num_decode)))
+    for s in picks:
+        prior, cnt = int(b.start_positions[s]), int(b.new_token_counts[s])
+        ctx = prior + cnt
+        rows = min(cnt, rows_per_chunk)
+        nb = -(-ctx // BS)
+        shape = (1, nb, BS, Hkv, D)
+        pos = prior + np.arange(rows, dtype=np.int64)
+        mask = (np.arange(ctx, dtype=np.int64)[None, :] <= pos[:, None]).astype(np.uint8)
+        flops = 4 * Hq * D * int((pos + 1).sum())
+        calls.append((bf16((1, Hq, rows, D)), bf16(shape), bf16(shape),
+                      np.arange(ctx, dtype=np.int32), mask.reshape(1, 1, rows, ctx), rows, flops))
+    return calls
+
+
+def run_cpu_calls(calls, scale, min_seconds=0.0):
+    """Run the sampled reference calls (one pass, or as many as fill `min_seconds`); returns
+    (new tokens/s, causal TFLOP/s, seconds per pass, kind, cores, passes)."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    if O.RefKernel.available():
+        k = O.RefKernel()
+        k.set_threads(cores)
+        call, kind = k.paged_attention, "reference"
+    else:
+        os.environ["OMP_NUM_THREADS"] = str(cores)
+        call, kind = O.paged_attention, "port"
+    rows = sum(c[5] for c in calls)
+    flops = sum(c[6] for c in calls)
+    t0 = time.perf_counter()
+    passes = 0
+    while passes < 1 or time.perf_counter() - t0 < min_seconds:
+        for q, kc, vc, gs, mask, _, _ in calls:
+            call(q, kc, vc, 0, gs, mask, scale)
+        passes += 1
+    dt = (time.perf_counter() - t0) / passes
+    return rows / dt, flops / dt / 1e12, dt, kind, cores, passes
+
+
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -494,6 +549,18 @@ def config3_arm(args):
         "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
         "device_status": paged_ops.read_status(dev),
     }
+    if not args.no_cpu:
+        npre_s = 16
+        calls = cpu_mixed_sample(full, npre_s)
+        tok_s, cpu_tf, dt, kind, cores, passes = run_cpu_calls(calls, full.scale,
+                                                               args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": round(tok_s, 1), "unit": "tokens/s", "cores": cores, "kind": kind,
+            "tflops": round(cpu_tf, 5),
+            "sample": (f"the {npre_s} prefill chunks (first 256 query rows of each, causal mask "
+                       f"over the chunk's whole context) and 16 of the decodes, one reference "
+                       f"call each, bf16 values upcast to fp32; {passes} pass(es), "
+                       f"{dt:.2f} s per pass")}
     print(json.dumps(line))
     return 0
 

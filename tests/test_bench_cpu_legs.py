@@ -1,0 +1,44 @@
+"""The CPU legs of bench.py: the config-3 reference sample is the causal arithmetic of the mixed
+step (its masks give the same rows as the oracle's ragged causal form) and its flop count is the
+GPU arm's algorithmic count when no rows are dropped."""
+import numpy as np
+
+import bench
+
+
+def _batch(pkg):
+    # 2 prefill chunks (one on a cached prefix) + 2 decodes, GQA 4/2, D 16, BS 4
+    return pkg.workloads.custom(seed=3, context_lens=[37, 21, 9, 14], new_token_counts=[12, 21, 1, 1],
+                                num_query_heads=4, num_kv_heads=2, head_dim=16, block_size=4)
+
+
+def test_mixed_sample_flops_match_the_gpu_arm_count(pkg):
+    b = _batch(pkg)
+    calls = bench.cpu_mixed_sample(b, num_prefill=2, rows_per_chunk=10 ** 6, num_decode=2)
+    assert len(calls) == 4
+    assert sum(c[5] for c in calls) == b.num_tokens
+    assert sum(c[6] for c in calls) == bench.attention_flops(b)
+
+
+def test_mixed_sample_masks_are_causal(pkg, oracle):
+    b = _batch(pkg)
+    calls = bench.cpu_mixed_sample(b, num_prefill=2, rows_per_chunk=8, num_decode=2)
+    for s, (q, kc, vc, gs, mask, rows, _) in enumerate(calls):
+        prior = int(b.start_positions[s])
+        assert rows == min(int(b.new_token_counts[s]), 8)
+        assert mask.shape == (1, 1, rows, prior + int(b.new_token_counts[s]))
+        out = oracle.paged_attention(q, kc, vc, 0, gs, mask, b.scale)[0]
+        ragged = oracle.paged_ragged(np.ascontiguousarray(q[0].transpose(1, 0, 2)), kc, vc, 0,
+                                     np.arange(kc.shape[1], dtype=np.int32)[None, :], [prior],
+                                     [rows], b.scale)
+        err = np.abs(out - ragged).max() / np.abs(ragged).max()
+        assert err <= 1e-5, (s, err)
+
+
+def test_run_cpu_calls_reports_rates(pkg):
+    b = _batch(pkg)
+    calls = bench.cpu_mixed_sample(b, num_prefill=2, num_decode=2)
+    tok_s, tflops, dt, kind, cores, passes = bench.run_cpu_calls(calls, b.scale)
+    assert passes == 1 and dt > 0 and cores >= 1
+    assert kind in ("reference", "port")
+    assert tok_s > 0 and tflops > 0
