@@ -140,8 +140,9 @@ int b200_paged_decode(const B200DecodeParams* p, void* workspace, size_t workspa
 #define B200_DECODE_STATIC_SCRATCH_BYTES ((size_t)64 << 20)
 int b200_paged_decode_static(const B200DecodeParams* p, void* stream);
 
-/* Split size of the decode plan, in tokens (multiple of 16); 0 restores the built-in heuristic
- * (512 tokens, halved while the batch would give fewer than 4 work items per SM). */
+/* Split size of the decode plan, in tokens (rounded up to a multiple of 16); 0 restores the
+ * built-in rule: 4096 tokens, halved (down to 64) while the batch would give fewer than 16
+ * (sequence, split, KV head) work items per SM, i.e. 8 per resident CTA. */
 void b200_set_decode_split_tokens(int32_t tokens);
 
 /* ============================================================================================

@@ -51,7 +51,9 @@ class DeviceBlockPool:
                                        device=self.device)
 
     def close(self) -> None:
+        """Free the pool's device memory; the ``tables`` view and the status view die with it."""
         if getattr(self, "_h", None):
+            self._tables = self._status = None
             N.lib().b200_pool_destroy(self._h)
             self._h = None
 
@@ -163,8 +165,10 @@ class DeviceBlockPool:
             gather = torch.empty(int(num_context_tokens), dtype=torch.int64, device=dev)
             out["gather_slots"] = gather
         for t in (seq_slots, start_positions, new_token_counts):
-            if t.dtype != torch.int32 or not t.is_cuda:
-                raise ValueError("seq_slots, start_positions, new_token_counts: int32 CUDA")
+            if (t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous() or
+                    t.numel() != S):
+                raise ValueError("seq_slots, start_positions, new_token_counts: contiguous int32 "
+                                 "CUDA tensors of one entry per sequence")
         with torch.cuda.device(dev):
             N.check(N.lib().b200_build_step_metadata(
                 self._h, seq_slots.data_ptr(), start_positions.data_ptr(),

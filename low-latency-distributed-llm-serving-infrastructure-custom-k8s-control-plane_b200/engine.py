@@ -106,6 +106,11 @@ class Scheduler:
         if blocks > self.allocator.get_total_blocks():
             raise ValueError(f"Sequence {seq.seq_id} requires {blocks} blocks but the KV cache "
                              f"pool has only {self.allocator.get_total_blocks()} blocks")
+        # the device pool's table rows have a fixed width (a host allocator has none)
+        row = getattr(self.kv, "max_blocks_per_seq", None)
+        if row is not None and blocks > row:
+            raise ValueError(f"Sequence {seq.seq_id} requires {blocks} blocks but a block table "
+                             f"row holds {row}")
         self.waiting.append(seq)
 
     def has_unfinished_sequences(self) -> bool:
@@ -137,6 +142,10 @@ class Scheduler:
         self.running = active
         budget = len(decodes)
         ignored: List[Sequence] = []
+        # the device pool has a fixed number of sequence slots (table rows): a sequence waits for
+        # one like it waits for blocks (a host allocator has no such limit)
+        free_slots = getattr(self.kv, "num_free_sequence_slots", None)
+        slots = free_slots() if free_slots is not None else None
         i = 0
         while i < len(self.waiting):
             seq = self.waiting[i]
@@ -144,12 +153,15 @@ class Scheduler:
             # max_batch_size bounds the decode group only (scheduler.py:94-96); admission is
             # limited by free blocks and the batched-token budget (:128-138)
             if (need > self.allocator.get_num_free_blocks()
-                    or budget + seq.total_len > self.max_num_batched_tokens):
+                    or budget + seq.total_len > self.max_num_batched_tokens
+                    or slots == 0):
                 ignored.append(seq)
                 i += 1
                 continue
             self.waiting.pop(i)
             self.kv.allocate_prefix_blocks(seq)
+            if slots is not None:
+                slots -= 1
             seq.status = SequenceStatus.RUNNING
             self.running.append(seq)
             prefills.append(seq)

@@ -90,6 +90,10 @@ class PagedKVCacheManager:
     def get_allocator(self) -> DeviceBlockPool:
         return self.pool
 
+    def num_free_sequence_slots(self) -> int:
+        """Sequence slots (rows of the device block tables) not held by a sequence."""
+        return len(self._free_slots)
+
     # ---- allocation (app/memory/manager.py:82-102) ---------------------------------------
     def init_sequence_table(self, seq) -> None:
         if seq.block_table is None:

@@ -42,13 +42,16 @@ def cache_geometry(key_cache: torch.Tensor) -> N.CacheGeometry:
 
 
 class Workspace:
-    """Grow-only device scratch buffer per device (256-byte aligned)."""
+    """Grow-only device scratch buffer per (device, stream), 256-byte aligned.  Keyed by stream
+    because the kernels of one call use the scratch until they finish: two streams sharing one
+    buffer would race, and a buffer replaced by a larger one is released in the order of the
+    stream that used it."""
 
     def __init__(self):
         self._buf = {}
 
-    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.type, device.index)
+    def get(self, device: torch.device, nbytes: int, stream: int) -> torch.Tensor:
+        key = (device.type, device.index, stream)
         buf = self._buf.get(key)
         if buf is None or buf.numel() < nbytes:
             buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
@@ -79,13 +82,47 @@ def read_status(device: torch.device, reset: bool = True) -> int:
     return v
 
 
-def decode_params(query, key_cache, value_cache, layer_idx, block_tables, context_lens, scale,
-                  out, max_context_len, query_rows=None, status=None) -> N.DecodeParams:
+def _check_attention_args(query, key_cache, value_cache, out, block_tables, context_lens,
+                          num_rows_needed) -> N.CacheGeometry:
+    """Shape and dtype rules the C ABI cannot see (its query and output carry no dtype or head
+    dim of their own: the kernels read them as the cache's).  ``num_rows_needed``: query rows the
+    kernels index directly (None when a row map places them)."""
     geom = cache_geometry(key_cache)
+    if value_cache.shape != key_cache.shape or value_cache.dtype != key_cache.dtype:
+        raise ValueError("value_cache must have the key cache's shape and dtype")
+    if not value_cache.is_contiguous():
+        raise ValueError("caches must be contiguous (L, NB, BS, Hkv, D)")
     if query.dim() != 3 or query.stride(-1) != 1:
         raise ValueError("query must be (rows, Hq, D) with the head dim contiguous")
+    if query.shape[2] != geom.head_dim:
+        raise ValueError(f"query head dim {query.shape[2]} != cache head dim {geom.head_dim}")
+    if query.dtype != key_cache.dtype:
+        raise ValueError(f"query dtype {query.dtype} must match the cache dtype {key_cache.dtype}")
+    if num_rows_needed is not None and query.shape[0] < num_rows_needed:
+        raise ValueError(f"query has {query.shape[0]} rows, the batch needs {num_rows_needed}")
+    if out is not None:
+        if out.dtype != key_cache.dtype:
+            raise ValueError(f"out dtype {out.dtype} must match the cache dtype {key_cache.dtype}")
+        if out.shape != query.shape or out.stride(-1) != 1:
+            raise ValueError("out must have the query's shape with the head dim contiguous")
     if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
         raise ValueError("block_tables and context_lens must be int32")
+    if block_tables.dim() not in (1, 2) or block_tables.stride(-1) != 1:
+        raise ValueError("block_tables must be (S, max_blocks) with unit stride along a row")
+    if context_lens.dim() != 1 or not context_lens.is_contiguous():
+        raise ValueError("context_lens must be a contiguous (S,) tensor")
+    if block_tables.dim() == 2 and block_tables.shape[0] < context_lens.shape[0]:
+        raise ValueError("block_tables has fewer rows than context_lens has sequences")
+    return geom
+
+
+def decode_params(query, key_cache, value_cache, layer_idx, block_tables, context_lens, scale,
+                  out, max_context_len, query_rows=None, status=None) -> N.DecodeParams:
+    geom = _check_attention_args(query, key_cache, value_cache, out, block_tables, context_lens,
+                                 context_lens.shape[0] if query_rows is None else None)
+    if query_rows is not None and (query_rows.dtype != torch.int32 or
+                                   query_rows.shape != context_lens.shape):
+        raise ValueError("query_rows must be int32 with one entry per sequence")
     p = N.DecodeParams()
     p.query = query.data_ptr()
     p.q_stride_row, p.q_stride_head = query.stride(0), query.stride(1)
@@ -114,17 +151,18 @@ def paged_decode(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torc
     """Decode attention (one new token per sequence) read through block tables (K1).
     query (rows, Hq, D); caches (L, NB, BS, Hkv, D); block_tables (S, max_blocks) int32;
     context_lens (S,) int32.  Returns out (rows, Hq, D) in the cache dtype."""
-    _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
     if out is None:
         out = torch.empty_like(query, dtype=key_cache.dtype)
-    st = status_word(query.device)
     p = decode_params(query, key_cache, value_cache, layer_idx, block_tables, context_lens, scale,
-                      out, max_context_len, query_rows, st)
+                      out, max_context_len, query_rows)
+    _require_cuda(query, key_cache, value_cache, block_tables, context_lens, query_rows, out)
+    p.status_word = status_word(query.device).data_ptr()
     L = N.lib()
+    stream = _stream(query.device)
     need = L.b200_paged_decode_workspace_bytes(ctypes.byref(p))
-    ws = workspace if workspace is not None else _WORKSPACE.get(query.device, need)
+    ws = workspace if workspace is not None else _WORKSPACE.get(query.device, need, stream)
     N.check(L.b200_paged_decode(ctypes.byref(p), ws.data_ptr() if need else None, ws.numel(),
-                                _stream(query.device)))
+                                stream))
     return out
 
 
@@ -134,10 +172,16 @@ def paged_prefill(query: torch.Tensor, key_cache: torch.Tensor, value_cache: tor
                   max_context_len: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Ragged causal attention through block tables (prefill chunks / mixed steps).
     query (Ntok, Hq, D); cu_seqlens (S+1,) int64; context_lens (S,) int32."""
-    _require_cuda(query, key_cache, value_cache, block_tables, cu_seqlens, context_lens)
     if out is None:
         out = torch.empty_like(query, dtype=key_cache.dtype)
-    geom = cache_geometry(key_cache)
+    geom = _check_attention_args(query, key_cache, value_cache, out, block_tables, context_lens,
+                                 None)
+    if block_tables.dim() != 2:
+        raise ValueError("block_tables must be (S, max_blocks)")
+    if (cu_seqlens.dtype != torch.int64 or cu_seqlens.dim() != 1 or
+            not cu_seqlens.is_contiguous() or cu_seqlens.numel() != context_lens.numel() + 1):
+        raise ValueError("cu_seqlens must be a contiguous int64 (S+1,) tensor")
+    _require_cuda(query, key_cache, value_cache, block_tables, cu_seqlens, context_lens, out)
     p = N.PrefillParams()
     p.query = query.data_ptr()
     p.q_stride_token, p.q_stride_head = query.stride(0), query.stride(1)
@@ -158,10 +202,11 @@ def paged_prefill(query: torch.Tensor, key_cache: torch.Tensor, value_cache: tor
     p.o_stride_token, p.o_stride_head = out.stride(0), out.stride(1)
     p.status_word = status_word(query.device).data_ptr()
     L = N.lib()
+    stream = _stream(query.device)
     need = L.b200_paged_prefill_workspace_bytes(ctypes.byref(p))
-    ws = _WORKSPACE.get(query.device, need) if need else None
+    ws = _WORKSPACE.get(query.device, need, stream) if need else None
     N.check(L.b200_paged_prefill(ctypes.byref(p), None if ws is None else ws.data_ptr(),
-                                 0 if ws is None else ws.numel(), _stream(query.device)))
+                                 0 if ws is None else ws.numel(), stream))
     return out
 
 

@@ -139,3 +139,48 @@ def test_tensor_parallel_sharding_matches_single_rank(pkg):
     np.testing.assert_allclose(l2, l1, rtol=1e-4, atol=1e-5)
     assert (t1 == t2).all()
     assert (t1 == l1.argmax(-1)).all()
+
+
+class SlottedKV(HostKV):
+    """HostKV with the device pool's two fixed limits: table rows of `row` blocks and `slots`
+    sequence slots."""
+
+    def __init__(self, la, total_blocks, block_size, row, slots):
+        super().__init__(la, total_blocks, block_size)
+        self.max_blocks_per_seq = row
+        self.slots = slots
+
+    def num_free_sequence_slots(self):
+        return self.slots
+
+    def allocate_prefix_blocks(self, seq):
+        if seq.block_table is None:
+            assert self.slots > 0, "admitted without a free sequence slot"
+            self.slots -= 1
+        super().allocate_prefix_blocks(seq)
+
+    def free_sequence(self, seq):
+        if seq.block_table is not None:
+            self.slots += 1
+        super().free_sequence(seq)
+
+
+def test_scheduler_respects_device_pool_limits(pkg):
+    from llm_serving_b200 import llm_allocator_cpp as la
+    from llm_serving_b200.engine import Scheduler, Sequence
+    kv = SlottedKV(la, total_blocks=64, block_size=4, row=3, slots=2)
+    sched = Scheduler(kv, max_batch_size=8, max_num_batched_tokens=1024, max_model_len=64)
+    with pytest.raises(ValueError, match="block table row"):
+        sched.add_sequence(Sequence(1, [1] * 9, max_tokens=4))    # 13 tokens = 4 blocks > 3
+    seqs = [Sequence(i, [1] * 3, max_tokens=2) for i in range(2, 6)]
+    for s in seqs:
+        sched.add_sequence(s)
+    out = sched.schedule()
+    assert [s.seq_id for s in out.scheduled_prefills] == [2, 3]   # two slots, two admissions
+    assert [s.seq_id for s in out.ignored_sequences] == [4, 5]
+    for s in out.scheduled_prefills:                               # both finish: slots come back
+        s.append_token(0)
+        s.append_token(0)
+        sched.free_sequence(s)
+    out = sched.schedule()
+    assert [s.seq_id for s in out.scheduled_prefills] == [4, 5]

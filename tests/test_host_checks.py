@@ -38,3 +38,63 @@ def test_graph_buckets_cover_batches(pkg):
     for n in range(1, 257):
         up = next(x for x in b if x >= n)
         assert up - n < 8
+
+
+def _decode_args(D=64, dtype=torch.bfloat16, q_dtype=None, q_dim=None, rows=3):
+    kc = torch.zeros((1, 4, 16, 2, D), dtype=dtype)
+    q = torch.zeros((rows, 4, q_dim or D), dtype=q_dtype or dtype)
+    bt = torch.zeros((3, 4), dtype=torch.int32)
+    ctx = torch.ones(3, dtype=torch.int32)
+    return q, kc, kc.clone(), bt, ctx
+
+
+def test_decode_refuses_a_query_the_kernels_would_misread(pkg):
+    """The C ABI reads the query as the cache's dtype and head dim: a mismatch must be refused
+    before any pointer reaches the library."""
+    from llm_serving_b200 import paged_ops
+    q, kc, vc, bt, ctx = _decode_args(q_dim=32)
+    with pytest.raises(ValueError, match="head dim"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, 0.125, 1)
+    q, kc, vc, bt, ctx = _decode_args(q_dtype=torch.float32)
+    with pytest.raises(ValueError, match="dtype"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, 0.125, 1)
+    q, kc, vc, bt, ctx = _decode_args(rows=2)
+    with pytest.raises(ValueError, match="rows"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, 0.125, 1)
+    q, kc, vc, bt, ctx = _decode_args()
+    with pytest.raises(ValueError, match="out"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, 0.125, 1, out=torch.zeros((3, 4, 32),
+                                                                                dtype=kc.dtype))
+    with pytest.raises(ValueError, match="value_cache"):
+        paged_ops.paged_decode(q, kc, vc[:, :2].contiguous(), 0, bt, ctx, 0.125, 1)
+    with pytest.raises(ValueError, match="int32"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt.long(), ctx, 0.125, 1)
+    with pytest.raises(ValueError, match="fewer rows"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt[:2], ctx, 0.125, 1)
+    # well-formed host tensors: refused for being on the host, never computed there
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        paged_ops.paged_decode(q, kc, vc, 0, bt, ctx, 0.125, 1)
+
+
+def test_prefill_checks_its_ragged_metadata(pkg):
+    from llm_serving_b200 import paged_ops
+    q, kc, vc, bt, ctx = _decode_args()
+    cu = torch.tensor([0, 1, 2, 3], dtype=torch.int64)
+    with pytest.raises(ValueError, match="cu_seqlens"):
+        paged_ops.paged_prefill(q, kc, vc, 0, bt, cu.int(), ctx, 0.125, 1, 1)
+    with pytest.raises(ValueError, match="cu_seqlens"):
+        paged_ops.paged_prefill(q, kc, vc, 0, bt, cu[:3], ctx, 0.125, 1, 1)
+    with pytest.raises(ValueError, match="head dim"):
+        paged_ops.paged_prefill(q[..., :32], kc, vc, 0, bt, cu, ctx, 0.125, 1, 1)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        paged_ops.paged_prefill(q, kc, vc, 0, bt, cu, ctx, 0.125, 1, 1)
+
+
+def test_workspace_is_per_stream(pkg):
+    from llm_serving_b200 import paged_ops
+    ws = paged_ops.Workspace()
+    cpu = torch.device("cpu")
+    a, b = ws.get(cpu, 1000, 1), ws.get(cpu, 1000, 2)
+    assert a.data_ptr() != b.data_ptr()
+    assert ws.get(cpu, 500, 1).data_ptr() == a.data_ptr()      # reused while large enough
+    assert ws.get(cpu, 4000, 1).numel() >= 4000                # grown when not
