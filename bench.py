@@ -842,6 +842,127 @@ def swap_arm(args):
     return 0
 
 
+def meta_arm(args):
+    """Per-step metadata (K4) at config-3 scale: cu_seqlens, context offsets and lengths,
+    position ids, slot mapping and padded block tables for 16 prefill chunks + 240 decodes, built
+    on the device from the device block pool's tables (a shuffled free list).  Device latency is
+    measured on a CUDA graph of one call replayed `--steps` times (the engine replays K4 inside
+    its decode graphs); the eager figure adds the host cost of one Python call.  The CPU
+    baseline is the numpy port of the reference's PagedStepContext + build_block_tables
+    (app/model/paged_attention.py:40-90, app/memory/manager.py:236-271) on the same tables."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200.block_manager import DeviceBlockPool
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    b = pkg.workloads.config3(seed=0)
+    S, BS = b.num_seqs, b.block_size
+    nfill = 64
+    per_fill = b.total_blocks // nfill
+    pool = DeviceBlockPool(b.total_blocks, BS, S + nfill, max(512, per_fill), dev)
+    rng = np.random.default_rng(0)
+    for i in range(nfill):                      # take the pool, give it back shuffled
+        pool.append_tokens(S + i, BS * per_fill)
+    pool.flush()
+    for i in rng.permutation(nfill):
+        pool.release(S + int(i))
+    pool.flush()
+    starts = b.start_positions.astype(np.int32)
+    counts = b.new_token_counts.astype(np.int32)
+    for s in range(S):
+        pool.append_tokens(s, int(starts[s] + counts[s]))
+    pool.flush()
+    bt_stride = max(pool.num_blocks(s) for s in range(S))
+    ntok = int(counts.sum())
+    nctx = int((starts + counts).sum())
+    d_slots = torch.arange(S, dtype=torch.int32, device=dev)
+    d_start = torch.from_numpy(starts).to(dev)
+    d_count = torch.from_numpy(counts).to(dev)
+
+    def call(gather):
+        return pool.build_step_metadata(d_slots, d_start, d_count, ntok, bt_stride=bt_stride,
+                                        with_gather_slots=gather, num_context_tokens=nctx)
+
+    def device_us(gather):
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            for _ in range(max(args.warmup, 3)):
+                call(gather)
+        cur.wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            md = call(gather)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1e3 / args.steps, md, g
+
+    us_engine, md, g1 = device_us(False)
+    us_full, md_full, g2 = device_us(True)
+    for _ in range(max(args.warmup, 3)):
+        call(True)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        call(True)
+    torch.cuda.synchronize(dev)
+    eager_us = (time.perf_counter() - t0) * 1e6 / args.steps
+    # bytes each call must move: the three per-sequence inputs and the pool's table rows read,
+    # the outputs written (gather slots only in the full variant)
+    base = 3 * S * 4 + S * bt_stride * 4 + 2 * (S + 1) * 8 + S * 4 + 2 * ntok * 8 + \
+        S * bt_stride * 4
+    line = {
+        "metric": "step metadata (K4) latency, config-3 step", "value": round(us_engine, 2),
+        "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": False, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": "config3 metadata: 16 prefill chunks + 240 decodes, BS 16, "
+                               "shuffled device pool", "num_seqs": S, "new_tokens": ntok,
+                   "context_tokens": nctx, "bt_stride": bt_stride},
+        "device_us": {"engine_outputs": round(us_engine, 2),
+                      "with_gather_slots": round(us_full, 2)},
+        "eager_us_with_gather_slots": round(eager_us, 2),
+        "bytes": {"engine_outputs": base, "with_gather_slots": base + nctx * 8},
+        "gpu_launches": 2 * args.steps,
+        "device_status": pool.status(),
+    }
+    if not args.no_cpu:
+        from oracle import oracle as O
+        tables = [pool.table(s) for s in range(S)]
+        tok = (starts + counts).tolist()
+        n = 0
+        t0 = time.perf_counter()
+        while n < 3 or time.perf_counter() - t0 < 2.0:
+            ref = O.step_metadata(tables, tok, starts.tolist(), counts.tolist(), BS)
+            ref_bt, _ = O.build_block_tables(tables, tok)
+            n += 1
+        cpu_us = (time.perf_counter() - t0) * 1e6 / n
+        exact = (np.array_equal(md_full["cu_seqlens"].cpu().numpy(), ref["cu_seqlens"]) and
+                 np.array_equal(md_full["cu_context_offsets"].cpu().numpy(),
+                                ref["cu_context_offsets"]) and
+                 np.array_equal(md_full["context_lens"].cpu().numpy(), ref["context_lens"]) and
+                 np.array_equal(md_full["position_ids"].cpu().numpy(), ref["position_ids"][0]) and
+                 np.array_equal(md_full["slot_mapping"].cpu().numpy(), ref["scatter_slots"]) and
+                 np.array_equal(md_full["gather_slots"].cpu().numpy(), ref["gather_slots"]) and
+                 np.array_equal(md_full["block_tables"].cpu().numpy(), ref_bt))
+        line["bit_exact_vs_port"] = bool(exact)
+        line["cpu_baseline"] = {
+            "value": round(cpu_us, 1), "unit": "us", "cores": 1, "kind": "port",
+            "sample": f"the whole step ({n} repetitions): numpy restatement of PagedStepContext "
+                      f"(scatter and gather slots, positions, offsets) + build_block_tables"}
+    del g1, g2
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -854,7 +975,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="minimum CPU work of the cpu_baseline leg (passes over the sample)")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap"],
+    ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
+                                           "meta"],
                     default="config2")
     ap.add_argument("--requests", type=int, default=200, help="engine4: requests to run")
     ap.add_argument("--rate", type=float, default=20.0, help="engine4: arrivals per second")
@@ -868,6 +990,8 @@ def main():
         return engine5_arm(args)
     if args.workload == "swap":
         return swap_arm(args)
+    if args.workload == "meta":
+        return meta_arm(args)
     if args.impl == "reference":
         return reference_arm(args)
     return ours_arm(args)

@@ -37,6 +37,8 @@ extern "C" {
 #define B200_DEVICE_BAD_SLOT 2    /* slot outside [0, total_blocks * block_size)            */
 #define B200_DEVICE_TIMEOUT 4     /* a bounded mbarrier wait expired                        */
 #define B200_DEVICE_BAD_OP 8      /* block-pool op inconsistent with the pool state         */
+#define B200_DEVICE_BAD_STEP 16   /* step metadata: bad sequence slot, negative start/count,
+                                     or more tokens than the outputs hold                   */
 
 /* ---- element types --------------------------------------------------------------------------- */
 #define B200_DTYPE_F32 0
@@ -309,13 +311,16 @@ int32_t b200_pool_snapshot_free(B200BlockPool* pool, int32_t* host_out, int32_t 
  *   position_ids (num_tokens) int64, slot_mapping (num_tokens) int64,
  *   block_tables (S, bt_stride) int32 padded with -1,
  *   gather_slots (num_context_tokens) int64 or NULL (only the masked-form kernel needs it).
+ * Every write stays inside these sizes: a sequence slot outside the pool, a negative start or
+ * count (the sequence then counts as empty), or counts whose sum overruns num_tokens /
+ * num_context_tokens set B200_DEVICE_BAD_STEP and the entries that do not fit are skipped.
  * Warp/block prefix sums; two launches. */
 int b200_build_step_metadata(const B200BlockPool* pool, const int32_t* seq_slots,
                              const int32_t* start_positions, const int32_t* new_token_counts,
                              int32_t num_seqs, int32_t num_tokens, int64_t* cu_seqlens,
                              int64_t* cu_context, int32_t* context_lens, int64_t* position_ids,
                              int64_t* slot_mapping, int32_t* block_tables, int32_t bt_stride,
-                             int64_t* gather_slots, void* stream);
+                             int64_t* gather_slots, int64_t num_context_tokens, void* stream);
 
 /* ============================================================================================
  * 6. Host mirror of the reference allocator API (PageAllocator / SequenceBlockTable)

@@ -26,6 +26,7 @@ DEVICE_BAD_BLOCK = 1
 DEVICE_BAD_SLOT = 2
 DEVICE_TIMEOUT = 4
 DEVICE_BAD_OP = 8
+DEVICE_BAD_STEP = 16
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -113,7 +114,8 @@ SIGNATURES = [
     ("b200_pool_status", c_vp, [c_vp]),
     ("b200_pool_snapshot_free", c_i32, [c_vp, ctypes.POINTER(c_i32), c_i32, c_vp]),
     ("b200_build_step_metadata", ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp,
-                                                c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp]),
+                                                c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_i64,
+                                                c_vp]),
     ("b200_host_allocator_create", ctypes.c_int, [c_i64, c_i64, c_i64, c_i64,
                                                   ctypes.POINTER(c_vp)]),
     ("b200_host_allocator_destroy", None, [c_vp]),

@@ -176,5 +176,6 @@ class DeviceBlockPool:
                 out["cu_context_offsets"].data_ptr(), out["context_lens"].data_ptr(),
                 out["position_ids"].data_ptr(), out["slot_mapping"].data_ptr(),
                 out["block_tables"].data_ptr(), bt_stride,
-                None if gather is None else gather.data_ptr(), _stream(dev)))
+                None if gather is None else gather.data_ptr(),
+                0 if gather is None else gather.numel(), _stream(dev)))
         return out

@@ -195,6 +195,10 @@ __global__ void __launch_bounds__(1024) meta_scan_kernel(MetaArgs a) {
     if (s < a.S) {
       n = a.counts[s];
       ctx = static_cast<int64_t>(a.starts[s]) + n;
+      if (n < 0 || ctx < n) {  // negative count or start: the sequence counts as empty
+        flag_status(a.status, B200_DEVICE_BAD_STEP);
+        n = ctx = 0;
+      }
       a.context_lens[s] = static_cast<int32_t>(ctx);
     }
     const int64_t eq = block_exclusive_scan_1024(n, warp_buf, &tot) + cq;
@@ -218,31 +222,43 @@ __global__ void __launch_bounds__(1024) meta_scan_kernel(MetaArgs a) {
   }
 }
 
-// K4 part 2: per-sequence fill (one CTA per sequence).
+// K4 part 2: per-sequence fill (one CTA per sequence).  Every write is bounded by its output's
+// size; what does not fit, or names a slot outside the pool, is flagged and skipped.
 __global__ void __launch_bounds__(256) meta_fill_kernel(MetaArgs a) {
   const int s = blockIdx.x;
   const int32_t slot = a.seq_slots[s];
-  const int32_t start = a.starts[s], count = a.counts[s];
+  int32_t start = a.starts[s], count = a.counts[s];
+  if (count < 0 || start < 0) start = count = 0;  // flagged by the scan
   const int64_t q0 = a.cu_seqlens[s];
-  const int32_t* trow = a.pool_tables + static_cast<int64_t>(slot) * a.pool_stride;
-  const int32_t owned = a.pool_nblocks[slot];
+  const bool slot_ok = slot >= 0 && slot < a.max_seqs;
+  if (!slot_ok && threadIdx.x == 0) flag_status(a.status, B200_DEVICE_BAD_STEP);
+  const int32_t* trow = a.pool_tables + (slot_ok ? static_cast<int64_t>(slot) * a.pool_stride : 0);
+  const int32_t owned = slot_ok ? min(a.pool_nblocks[slot], a.pool_stride) : 0;
   for (int i = threadIdx.x; i < a.bt_stride; i += blockDim.x)
     a.block_tables[static_cast<int64_t>(s) * a.bt_stride + i] = i < owned ? trow[i] : -1;
-  for (int i = threadIdx.x; i < count; i += blockDim.x) {
-    const int32_t pos = start + i;
-    a.position_ids[q0 + i] = pos;
-    const int32_t bi = pos / a.bs;
-    const int32_t b = bi < owned ? trow[bi] : -1;
-    if (b < 0 || b >= a.nb) {
-      flag_status(a.status, B200_DEVICE_BAD_BLOCK);
-      a.slot_mapping[q0 + i] = -1;
-    } else {
-      a.slot_mapping[q0 + i] = static_cast<int64_t>(b) * a.bs + pos % a.bs;
+  if (q0 < 0 || q0 + count > a.max_tokens) {
+    if (threadIdx.x == 0) flag_status(a.status, B200_DEVICE_BAD_STEP);
+  } else {
+    for (int i = threadIdx.x; i < count; i += blockDim.x) {
+      const int32_t pos = start + i;
+      a.position_ids[q0 + i] = pos;
+      const int32_t bi = pos / a.bs;
+      const int32_t b = bi < owned ? trow[bi] : -1;
+      if (b < 0 || b >= a.nb) {
+        flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+        a.slot_mapping[q0 + i] = -1;
+      } else {
+        a.slot_mapping[q0 + i] = static_cast<int64_t>(b) * a.bs + pos % a.bs;
+      }
     }
   }
   if (a.gather_slots != nullptr) {
     const int64_t c0 = a.cu_context[s];
     const int32_t ctx = start + count;
+    if (c0 < 0 || c0 + ctx > a.max_ctx) {
+      if (threadIdx.x == 0) flag_status(a.status, B200_DEVICE_BAD_STEP);
+      return;
+    }
     for (int p = threadIdx.x; p < ctx; p += blockDim.x) {
       const int32_t bi = p / a.bs;
       const int32_t b = bi < owned ? trow[bi] : -1;

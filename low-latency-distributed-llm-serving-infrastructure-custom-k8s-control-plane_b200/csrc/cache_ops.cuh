@@ -109,6 +109,9 @@ struct MetaArgs {
   int32_t bt_stride;
   int64_t* gather_slots;
   int32_t* status;
+  int32_t max_seqs;      // pool slots: seq_slots entries must lie in [0, max_seqs)
+  int64_t max_tokens;    // entries of position_ids / slot_mapping
+  int64_t max_ctx;       // entries of gather_slots
 };
 
 cudaError_t launch_step_metadata(const MetaArgs& a, cudaStream_t stream);

@@ -329,11 +329,10 @@ int b200_build_step_metadata(const B200BlockPool* pool, const int32_t* seq_slots
                              int32_t num_seqs, int32_t num_tokens, int64_t* cu_seqlens,
                              int64_t* cu_context, int32_t* context_lens, int64_t* position_ids,
                              int64_t* slot_mapping, int32_t* block_tables, int32_t bt_stride,
-                             int64_t* gather_slots, void* stream) {
+                             int64_t* gather_slots, int64_t num_context_tokens, void* stream) {
   if (pool == nullptr) return pfail(B200_ERR_INVALID_ARGUMENT, "null pool");
-  if (num_seqs < 0 || num_tokens < 0 || bt_stride < 0)
+  if (num_seqs < 0 || num_tokens < 0 || bt_stride < 0 || num_context_tokens < 0)
     return pfail(B200_ERR_INVALID_ARGUMENT, "negative sizes");
-  (void)num_tokens;
   b200::MetaArgs a{};
   a.seq_slots = seq_slots;
   a.starts = start_positions;
@@ -353,6 +352,9 @@ int b200_build_step_metadata(const B200BlockPool* pool, const int32_t* seq_slots
   a.bt_stride = bt_stride;
   a.gather_slots = gather_slots;
   a.status = pool->d_status;
+  a.max_seqs = pool->max_seqs;
+  a.max_tokens = num_tokens;
+  a.max_ctx = gather_slots != nullptr ? num_context_tokens : 0;
   if (b200::launch_step_metadata(a, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return pfail(B200_ERR_CUDA, "step metadata launch failed");
   return B200_OK;

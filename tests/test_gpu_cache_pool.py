@@ -184,3 +184,77 @@ def test_step_metadata_config3_scale(pkg, bm, oracle):
     assert np.array_equal(md["position_ids"].cpu().numpy(), ref["position_ids"][0])
     bt, _ = oracle.build_block_tables(tables, (starts + counts).tolist())
     assert np.array_equal(md["block_tables"].cpu().numpy(), bt)
+
+
+def _raw_metadata(pool, slots, starts, counts, num_tokens, room, bt_stride,
+                  num_context_tokens=None, ctx_room=0):
+    """b200_build_step_metadata called directly, with outputs `room` entries longer than the
+    capacity the call declares and filled with a sentinel, so what lands past the capacity is
+    visible (and stays inside memory this test owns)."""
+    from llm_serving_b200 import _native as N
+    dev = torch.device("cuda")
+    S = len(slots)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
+    d_slots, d_start, d_count = i32(slots), i32(starts), i32(counts)
+    out = {
+        "cu": torch.full((S + 1,), -7, dtype=torch.int64, device=dev),
+        "cc": torch.full((S + 1,), -7, dtype=torch.int64, device=dev),
+        "ctx": torch.full((S,), -7, dtype=torch.int32, device=dev),
+        "pos": torch.full((num_tokens + room,), -7, dtype=torch.int64, device=dev),
+        "slot": torch.full((num_tokens + room,), -7, dtype=torch.int64, device=dev),
+        "bt": torch.full((S, bt_stride), -7, dtype=torch.int32, device=dev),
+    }
+    gather = None
+    if num_context_tokens is not None:
+        gather = torch.full((num_context_tokens + ctx_room,), -7, dtype=torch.int64, device=dev)
+    N.check(N.lib().b200_build_step_metadata(
+        pool._h, d_slots.data_ptr(), d_start.data_ptr(), d_count.data_ptr(), S, num_tokens,
+        out["cu"].data_ptr(), out["cc"].data_ptr(), out["ctx"].data_ptr(), out["pos"].data_ptr(),
+        out["slot"].data_ptr(), out["bt"].data_ptr(), bt_stride,
+        None if gather is None else gather.data_ptr(),
+        0 if gather is None else num_context_tokens, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out, gather
+
+
+def test_step_metadata_stays_inside_its_outputs(bm):
+    """Counts that overrun the declared output sizes, a sequence slot outside the pool and a
+    negative count are flagged (B200_DEVICE_BAD_STEP) and skipped; nothing is written past the
+    capacities, and the consistent sequences still get exact metadata."""
+    from llm_serving_b200 import _native as N
+    pool = bm.DeviceBlockPool(32, 16, max_seqs=4, max_blocks_per_seq=8)
+    pool.append_tokens(0, 20)
+    pool.append_tokens(1, 40)
+    pool.flush()
+    t0, t1 = pool.table(0), pool.table(1)
+    assert pool.status() == 0
+
+    # 1. the second sequence's 25 tokens do not fit a 30-token capacity after the first's 10
+    out, _ = _raw_metadata(pool, [0, 1], [10, 15], [10, 25], num_tokens=30, room=8, bt_stride=4)
+    assert pool.status() & N.DEVICE_BAD_STEP
+    assert out["pos"][:10].tolist() == list(range(10, 20))
+    assert out["slot"][:10].tolist() == [t0[p // 16] * 16 + p % 16 for p in range(10, 20)]
+    assert (out["pos"][10:] == -7).all() and (out["slot"][10:] == -7).all()
+    assert out["cu"].tolist() == [0, 10, 35] and out["ctx"].tolist() == [20, 40]
+    assert out["bt"][1].tolist() == t1 + [-1]
+
+    # 2. gather slots: a 50-entry capacity holds the first sequence's 20, not the second's 40
+    out, g = _raw_metadata(pool, [0, 1], [19, 39], [1, 1], num_tokens=2, room=0, bt_stride=3,
+                           num_context_tokens=50, ctx_room=16)
+    assert pool.status() & N.DEVICE_BAD_STEP
+    assert g[:20].tolist() == [t0[p // 16] * 16 + p % 16 for p in range(20)]
+    assert (g[20:] == -7).all()
+
+    # 3. a slot outside the pool and a negative count: flagged, treated as empty sequences
+    out, _ = _raw_metadata(pool, [7, 1, 0], [0, 39, 0], [1, 1, -3], num_tokens=2, room=4,
+                           bt_stride=3)
+    st = pool.status()
+    assert st & N.DEVICE_BAD_STEP and st & N.DEVICE_BAD_BLOCK
+    assert out["bt"][0].tolist() == [-1, -1, -1] and out["slot"][0].item() == -1
+    assert out["pos"][1].item() == 39 and out["slot"][1].item() == t1[2] * 16 + 39 % 16
+    assert out["cu"].tolist() == [0, 1, 2, 2] and out["ctx"][2].item() == 0
+    assert (out["pos"][2:] == -7).all()
+
+    # a consistent call afterwards is clean
+    _raw_metadata(pool, [0, 1], [19, 39], [1, 1], num_tokens=2, room=0, bt_stride=3)
+    assert pool.status() == 0
