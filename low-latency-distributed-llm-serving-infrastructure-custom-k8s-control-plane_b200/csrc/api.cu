@@ -1,5 +1,6 @@
 // C ABI of libb200paged.so (include/b200_paged.h): argument validation, plans, tensor maps and
 // kernel launches.  No torch types; every entry point works on raw device pointers and a stream.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -33,13 +34,19 @@ int esize_of(int dtype) {
   }
 }
 
+// SM count of the calling thread's current device, cached per device (calls may come from
+// several threads and devices).
 int num_sms() {
-  static int n = 0;
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>* slot = (dev >= 0 && dev < kMaxDevices) ? &cache[dev] : nullptr;
+  int n = slot ? slot->load(std::memory_order_relaxed) : 0;
   if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
+    if (slot) slot->store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -120,8 +127,9 @@ int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows
   return B200_OK;
 }
 
-int g_split_override = 0;
-bool g_force_cuda_core_prefill = false;
+// Process-wide tuning knobs (b200_set_decode_split_tokens, b200_set_prefill_cuda_cores).
+std::atomic<int> g_split_override{0};
+std::atomic<bool> g_force_cuda_core_prefill{false};
 
 struct DecodePlan {
   bool tensor_cores;
@@ -174,7 +182,7 @@ DecodePlan make_decode_plan(const B200DecodeParams& p) {
   // (2 per SM) for the work stealing to balance the tail.  Measured on config 2 (256 sequences,
   // lognormal contexts <= 4096): split 256 / 512 / 1024 / 2048 / 4096 reach 61 / 78 / 88 / 91 /
   // 89 % of the HBM copy peak; this rule picks 2048 there.
-  int split = g_split_override;
+  int split = g_split_override.load(std::memory_order_relaxed);
   if (split <= 0) {
     split = 4096;
     while (split > 64 &&
@@ -224,7 +232,7 @@ const char* b200_status_string(int status) {
 const char* b200_last_error(void) { return g_last_error.c_str(); }
 
 void b200_set_decode_split_tokens(int32_t tokens) {
-  g_split_override = tokens > 0 ? ((tokens + 15) / 16) * 16 : 0;
+  g_split_override.store(tokens > 0 ? ((tokens + 15) / 16) * 16 : 0, std::memory_order_relaxed);
 }
 
 // ---- reference-signature masked attention ---------------------------------------------------
@@ -520,7 +528,7 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int G = p.num_query_heads / p.geom.num_kv_heads;
   const PrefillPlan pl = make_prefill_plan(p);
-  if (pl.tensor_cores && !g_force_cuda_core_prefill) {
+  if (pl.tensor_cores && !g_force_cuda_core_prefill.load(std::memory_order_relaxed)) {
     if (workspace == nullptr || workspace_bytes < pl.total)
       return fail(B200_ERR_INVALID_ARGUMENT, "prefill workspace too small");
     if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
@@ -612,7 +620,9 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
   return B200_OK;
 }
 
-void b200_set_prefill_cuda_cores(int32_t enable) { g_force_cuda_core_prefill = enable != 0; }
+void b200_set_prefill_cuda_cores(int32_t enable) {
+  g_force_cuda_core_prefill.store(enable != 0, std::memory_order_relaxed);
+}
 
 // ---- reshape_and_cache ------------------------------------------------------------------------
 
