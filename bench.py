@@ -593,13 +593,8 @@ def engine4_arm(args):
     from llm_serving_b200.engine import build_engine
     from llm_serving_b200.model import CONFIG4, kv_bytes_per_token
     world, rank, dev = _dist_setup()
-    rng = np.random.default_rng(4)
-    n_all = 2000
-    gaps = rng.exponential(1.0 / args.rate, size=n_all)
-    arrivals = np.cumsum(gaps) - gaps[0]
-    plens = np.clip(np.rint(np.exp(rng.normal(math.log(512), 0.8, size=n_all))), 1, 4096).astype(int)
-    olens = rng.integers(64, 513, size=n_all)
-    prompts = [rng.integers(0, CONFIG4.vocab, size=int(L)).tolist() for L in plens[:args.requests]]
+    arrivals, prompts, olens = pkg.workloads.config4_requests(args.requests, args.rate,
+                                                              CONFIG4.vocab)
     nreq = args.requests
     blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(CONFIG4, world) * 16))
     eng = build_engine(CONFIG4, total_blocks=blocks, block_size=16, rank=rank, world=world,

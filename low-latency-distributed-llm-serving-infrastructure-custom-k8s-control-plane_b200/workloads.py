@@ -151,3 +151,19 @@ def custom(seed: int, context_lens, new_token_counts, num_query_heads: int, num_
                       ctx - cnt, cnt, tables,
                       scale if scale is not None else 1.0 / math.sqrt(head_dim), dtype, seed,
                       free)
+
+
+def config4_requests(num: int, rate: float = 20.0, vocab: int = 32000, seed: int = 4,
+                     total: int = 2000):
+    """Config 4's request stream: `total` requests with Poisson arrivals at `rate` per second
+    (first at t=0), prompt lengths lognormal(median 512, sigma 0.8) clipped to [1, 4096] of
+    uniform token ids, output lengths uniform in [64, 512].  Returns (arrival times (total,),
+    prompts of the first `num` requests, output lengths (total,))."""
+    rng = np.random.default_rng(seed)
+    gaps = rng.exponential(1.0 / rate, size=total)
+    arrivals = np.cumsum(gaps) - gaps[0]
+    plens = np.clip(np.rint(np.exp(rng.normal(math.log(512), 0.8, size=total))), 1,
+                    4096).astype(int)
+    olens = rng.integers(64, 513, size=total)
+    prompts = [rng.integers(0, vocab, size=int(L)).tolist() for L in plens[:num]]
+    return arrivals, prompts, olens

@@ -42,3 +42,19 @@ def test_run_cpu_calls_reports_rates(pkg):
     assert passes == 1 and dt > 0 and cores >= 1
     assert kind in ("reference", "port")
     assert tok_s > 0 and tflops > 0
+
+
+def test_config4_request_stream_is_the_seeded_one(pkg):
+    """The engine bench's request stream: seed 4, draws in the order arrivals, prompt lengths,
+    output lengths, then the prompts' token ids."""
+    import math
+    arrivals, prompts, olens = pkg.workloads.config4_requests(5)
+    rng = np.random.default_rng(4)
+    gaps = rng.exponential(1.0 / 20.0, size=2000)
+    plens = np.clip(np.rint(np.exp(rng.normal(math.log(512), 0.8, size=2000))), 1, 4096)
+    expect_olens = rng.integers(64, 513, size=2000)
+    assert arrivals[0] == 0.0 and np.allclose(np.diff(arrivals), gaps[1:])
+    assert np.array_equal(olens, expect_olens)
+    assert [len(p) for p in prompts] == plens[:5].astype(int).tolist()
+    assert prompts[0] == rng.integers(0, 32000, size=int(plens[0])).tolist()
+    assert 64 <= olens.min() and olens.max() <= 512 and max(map(max, prompts)) < 32000
