@@ -1,8 +1,6 @@
 """Helpers for reading the ragged entries of tests/golden/golden.npz."""
 import json
 
-import numpy as np
-
 
 def ragged(golden, prefix):
     flat = golden[prefix + "tables_flat"]
