@@ -275,8 +275,10 @@ int b200_pool_share(B200BlockPool* pool, int32_t dst_slot, int32_t src_slot, int
  * list and the old block loses an owner (allocate_block + SequenceBlockTable::replace_block +
  * free_block, page_allocator.hpp:100-127, :416-424, :151-177).  After the flush,
  * b200_pool_cow_pairs gives the (old, new) block ids of every replacement of that flush as two
- * device arrays, ready for b200_copy_blocks (so the copy needs no host round trip).  Replace only
- * blocks that have another owner: a sole owner's old block would be freed in the same flush. */
+ * device arrays, ready for b200_copy_blocks (so the copy needs no host round trip); they hold
+ * that flush's pairs until the next b200_pool_flush, which may also reallocate them, so enqueue
+ * the copy before flushing again.  Replace only blocks that have another owner: a sole owner's
+ * old block would be freed in the same flush. */
 int b200_pool_copy_on_write(B200BlockPool* pool, int32_t slot, int32_t block_index);
 int32_t b200_pool_cow_pairs(const B200BlockPool* pool, const int32_t** old_blocks,
                             const int32_t** new_blocks);
