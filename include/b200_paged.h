@@ -101,7 +101,8 @@ typedef struct {
   const void* query;      /* one row per sequence: [row][Hq][D] with the strides below     */
   int64_t q_stride_row;   /* elements between query rows                                   */
   int64_t q_stride_head;  /* elements between heads of a row (D contiguous)                */
-  const int32_t* query_rows; /* (S,) row of each sequence's query/output; NULL = row s     */
+  const int32_t* query_rows; /* (S,) row of each sequence's query/output; NULL = row s;   */
+                             /* each entry must be a row of both query and out          */
   const void* key_cache;
   const void* value_cache;
   B200CacheGeometry geom;
