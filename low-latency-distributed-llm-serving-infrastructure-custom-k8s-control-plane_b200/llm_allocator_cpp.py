@@ -10,6 +10,9 @@
                             -> CUDA tensor out, with no copies; numpy arrays or CPU tensors are
                             copied to the GPU and the result is returned as numpy, as the
                             reference returns it.  There is no CPU execution path.
+* ``paged_attention_decode``, ``paged_prefill``, ``reshape_and_cache``, ``build_step_metadata``
+  and ``DeviceBlockPool`` -- the torch-tensor entry points of the B200 path (device tensors,
+  an optional stream), for callers that bind this module rather than the package.
 """
 from __future__ import annotations
 
@@ -189,3 +192,70 @@ def paged_attention(query, key_cache, value_cache, layer_idx, gather_slots, atte
     if on_device:
         return out
     return out.cpu().numpy()
+
+
+# ---- torch-tensor entry points of the B200 path ---------------------------------------------
+# Device tensors in, device tensors out, enqueued on `stream` (a torch.cuda.Stream, a raw
+# cudaStream_t handle, or None for the current stream).  None of them needs a host upper bound
+# read from the device: the context bound is the block tables' width times the block size.
+
+def _on_stream(stream, device):
+    import contextlib
+
+    import torch
+    if stream is None:
+        return contextlib.nullcontext()
+    if isinstance(stream, int):
+        stream = torch.cuda.ExternalStream(stream, device=device)
+    return torch.cuda.stream(stream)
+
+
+def _context_bound(block_tables, key_cache) -> int:
+    return int(block_tables.shape[-1]) * int(key_cache.shape[2])
+
+
+def paged_attention_decode(query, key_cache, value_cache, layer_idx, block_tables, context_lens,
+                           scale, out=None, stream=None):
+    """Decode attention through block tables: query (S, Hq, D), caches (L, NB, BS, Hkv, D),
+    block_tables (S, max_blocks) int32, context_lens (S,) int32 -> out (S, Hq, D)."""
+    from .paged_ops import paged_decode
+    with _on_stream(stream, query.device):
+        return paged_decode(query, key_cache, value_cache, int(layer_idx), block_tables,
+                            context_lens, float(scale), _context_bound(block_tables, key_cache),
+                            out=out)
+
+
+def paged_prefill(query, key_cache, value_cache, layer_idx, block_tables, cu_seqlens,
+                  context_lens, scale, out=None, stream=None):
+    """Ragged causal attention (prefill chunks and mixed steps): query (Ntok, Hq, D),
+    cu_seqlens (S+1,) int64, context_lens (S,) int32 -> out (Ntok, Hq, D)."""
+    from .paged_ops import paged_prefill as _prefill
+    with _on_stream(stream, query.device):
+        return _prefill(query, key_cache, value_cache, int(layer_idx), block_tables, cu_seqlens,
+                        context_lens, float(scale), int(query.shape[0]),
+                        _context_bound(block_tables, key_cache), out=out)
+
+
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, layer_idx, stream=None):
+    """key/value (Ntok, Hkv, D) -> their cache slots (slot_mapping (Ntok,) int64)."""
+    from .paged_ops import reshape_and_cache as _write
+    with _on_stream(stream, key.device):
+        _write(key, value, key_cache, value_cache, slot_mapping, int(layer_idx))
+
+
+def build_step_metadata(pool, seq_slots, start_positions, new_token_counts, num_tokens,
+                        bt_stride=None, stream=None):
+    """Per-step metadata on the device from a DeviceBlockPool: cu_seqlens, cu_context_offsets,
+    context_lens, position_ids, slot_mapping and padded block_tables, as a dict of tensors."""
+    with _on_stream(stream, pool.device):
+        return pool.build_step_metadata(seq_slots, start_positions, new_token_counts,
+                                        int(num_tokens), bt_stride=bt_stride)
+
+
+def __getattr__(name):
+    # the device block pool, imported on first use (it needs torch; the allocator classes above
+    # do not)
+    if name == "DeviceBlockPool":
+        from .block_manager import DeviceBlockPool
+        return DeviceBlockPool
+    raise AttributeError(name)

@@ -98,3 +98,25 @@ def test_workspace_is_per_stream(pkg):
     assert a.data_ptr() != b.data_ptr()
     assert ws.get(cpu, 500, 1).data_ptr() == a.data_ptr()      # reused while large enough
     assert ws.get(cpu, 4000, 1).numel() >= 4000                # grown when not
+
+
+def test_dropin_module_has_the_tensor_entry_points(pkg):
+    """The drop-in llm_allocator_cpp module carries the torch-tensor entry points of the B200
+    path next to the reference's classes, and they refuse host tensors (no CPU fallback)."""
+    from llm_serving_b200 import block_manager
+    from llm_serving_b200 import llm_allocator_cpp as la
+    for name in ("paged_attention_decode", "paged_prefill", "reshape_and_cache",
+                 "build_step_metadata"):
+        assert callable(getattr(la, name))
+    assert la.DeviceBlockPool is block_manager.DeviceBlockPool
+    q, kc, vc, bt, ctx = _decode_args()
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        la.paged_attention_decode(q, kc, vc, 0, bt, ctx, 0.125)
+    with pytest.raises(ValueError, match="head dim"):
+        la.paged_attention_decode(q[..., :32], kc, vc, 0, bt, ctx, 0.125)
+    cu = torch.tensor([0, 1, 2, 3], dtype=torch.int64)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        la.paged_prefill(q, kc, vc, 0, bt, cu, ctx, 0.125)
+    k = torch.zeros((3, 2, 64), dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        la.reshape_and_cache(k, k.clone(), kc, vc, cu[:3], 0)
