@@ -239,3 +239,26 @@ def test_prefill_config3_subset(pkg, oracle, ops):
                              new_token_counts=full.new_token_counts[idx], num_query_heads=32,
                              num_kv_heads=8, head_dim=128, block_size=16)
     _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=4)
+
+
+def test_masked_kernel_random_masks(oracle, ops):
+    """The reference-signature kernel on arbitrary masks (a fully masked row gives zeros), fp32,
+    against the oracle within 1e-5 relative."""
+    rng = np.random.default_rng(17)
+    hkv, hq, d, bs, NB = 2, 6, 64, 16, 12
+    nq, nctx = 9, 150
+    kc = rng.standard_normal((2, NB, bs, hkv, d), dtype=np.float32)
+    vc = rng.standard_normal((2, NB, bs, hkv, d), dtype=np.float32)
+    q = rng.standard_normal((1, hq, nq, d), dtype=np.float32)
+    gs = rng.permutation(NB * bs)[:nctx].astype(np.int32)
+    mask = (rng.random((1, 1, nq, nctx)) < 0.3).astype(np.uint8)
+    mask[0, 0, 4] = 0
+    mask[0, 0, 7] = 1
+    ref = oracle.paged_attention(q, kc, vc, 1, gs, mask, 0.125)
+    dev = torch.device("cuda")
+    out = ops.paged_attention_masked(torch.from_numpy(q).to(dev), torch.from_numpy(kc).to(dev),
+                                     torch.from_numpy(vc).to(dev), 1, torch.from_numpy(gs).to(dev),
+                                     torch.from_numpy(mask).to(dev), 0.125).cpu().numpy()
+    assert max_rel(out, ref) <= FP32_REL
+    assert not out[0, 4].any()
+    assert ops.read_status(dev) == 0

@@ -185,3 +185,27 @@ def test_empty_context_gives_zeros(oracle):
     out = oracle.paged_attention(q, kc, kc, 0, np.zeros(0, np.int32), np.zeros((1, 1, 3, 0), np.uint8),
                                  0.5)
     assert out.shape == (1, 3, 2, 8) and not out.any()
+
+
+@pytest.mark.skipif(not __import__("os").path.exists(
+    __import__("os").path.join(__import__("os").path.dirname(__file__), "..", "oracle", "_ref",
+                               "libref_paged_kernels.so")), reason="compiled reference absent")
+def test_oracle_matches_compiled_reference_random_masks(oracle):
+    """Arbitrary masks (not block-diagonal causal), with a fully masked row and a fully open one:
+    the oracle stays bit-exact to the reference kernel, and a fully masked row is zeros
+    (paged_kernels.cpp:27-104)."""
+    ref = oracle.RefKernel()
+    rng = np.random.default_rng(17)
+    hkv, hq, d, bs, NB = 2, 6, 16, 4, 12
+    nq, nctx = 7, 30
+    kc = rng.standard_normal((1, NB, bs, hkv, d), dtype=np.float32)
+    vc = rng.standard_normal((1, NB, bs, hkv, d), dtype=np.float32)
+    q = rng.standard_normal((1, hq, nq, d), dtype=np.float32)
+    gs = rng.permutation(NB * bs)[:nctx].astype(np.int32)
+    mask = (rng.random((1, 1, nq, nctx)) < 0.4).astype(np.uint8)
+    mask[0, 0, 2] = 0
+    mask[0, 0, 5] = 1
+    r = ref.paged_attention(q, kc, vc, 0, gs, mask, 0.3)
+    o = oracle.paged_attention(q, kc, vc, 0, gs, mask, 0.3)
+    np.testing.assert_array_equal(o, r)
+    assert not o[0, 2].any() and np.isfinite(o).all()
