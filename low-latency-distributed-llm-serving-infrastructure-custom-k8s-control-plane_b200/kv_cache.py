@@ -217,6 +217,27 @@ class PagedKVCacheManager:
         return self.value_cache[layer_idx].view(-1, self.num_heads, self.head_dim).index_select(
             0, slot_indices.to(self._device))
 
+    def gather_kv_cache(self, seq, read_len: Optional[int] = None):
+        """The sequence's first ``read_len`` tokens (default: all it holds) of every layer as
+        ``((key, value), ...)`` in the HF past-key-value layout (1, Hkv, read_len, D), gathered
+        from its blocks (manager.py:207-234); None without a block table or for read_len <= 0."""
+        if seq.block_table is None:
+            return None
+        blocks = seq.block_table.get_physical_blocks()
+        if read_len is None:
+            read_len = seq.block_table.get_tokens_count()
+        if read_len <= 0:
+            return None
+        ids = torch.tensor(blocks, dtype=torch.long, device=self._device)
+        out = []
+        for layer in range(self.num_layers):
+            k = self.key_cache[layer].index_select(0, ids).reshape(-1, self.num_heads,
+                                                                    self.head_dim)[:read_len]
+            v = self.value_cache[layer].index_select(0, ids).reshape(-1, self.num_heads,
+                                                                      self.head_dim)[:read_len]
+            out.append((k.unsqueeze(0).transpose(1, 2), v.unsqueeze(0).transpose(1, 2)))
+        return tuple(out)
+
     def write_prefix_kv(self, seq, keys: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
         if keys.shape != values.shape:
             raise ValueError(f"Keys shape {keys.shape} != Values shape {values.shape}")

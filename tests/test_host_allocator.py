@@ -177,3 +177,14 @@ def test_random_ops_match_oracle_fifo(la, oracle):
             a.free_block(b)
             f.free_block(b)
         assert a.get_num_free_blocks() == f.get_num_free_blocks()
+
+
+def test_block_size_counts_tokens_not_bytes(la):
+    """tokens_per_block is the block size; the host swap pool is sized in bytes from it
+    (the reference's test_block_size_is_tokens_not_bytes)."""
+    bytes_per_token = 2 * 8 * 4 * 2            # heads x head_dim x fp32 x (K and V)
+    a = la.PageAllocator(total_blocks=10, tokens_per_block=4, bytes_per_token=bytes_per_token,
+                         total_cpu_blocks=32)
+    assert a.get_block_size() == 4
+    assert a.get_bytes_per_token() == bytes_per_token
+    assert a.get_host_pool_bytes() == 32 * 4 * bytes_per_token
