@@ -120,3 +120,30 @@ def test_dropin_module_has_the_tensor_entry_points(pkg):
     k = torch.zeros((3, 2, 64), dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         la.reshape_and_cache(k, k.clone(), kc, vc, cu[:3], 0)
+
+
+def test_backend_selection_names(pkg, monkeypatch):
+    """The reference's backend names (attention_backends.py:126-144): 'native' and its 'hip'
+    alias, 'auto'; 'torch' (the reference's own SDPA backend) and unknown names are refused."""
+    from llm_serving_b200 import attention_backends as ab
+    with pytest.raises(ValueError, match="reference"):
+        ab.select_backend("torch")
+    with pytest.raises(ValueError, match="Unsupported"):
+        ab.select_backend("bogus")
+    backend = ab.NativePagedBackend()
+    assert backend.supports(None, 5) and not backend.supports(None, 0)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_backend_selection_without_a_device_fails_loudly(pkg, monkeypatch):
+    """Without a CUDA device every name that resolves to the native backend raises; 'auto' does
+    not fall back to a host path."""
+    from llm_serving_b200 import attention_backends as ab
+    for name in ("native", "hip", "auto"):
+        with pytest.raises(RuntimeError, match="CUDA device"):
+            ab.select_backend(name)
+    monkeypatch.setenv(ab.BACKEND_ENV_VAR, "hip")
+    with pytest.raises(RuntimeError):
+        ab.select_backend()
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        ab.NativePagedBackend().attend(torch.zeros(1, 2, 1, 8), None, 0, None, 1.0, 0.0)
