@@ -209,3 +209,36 @@ def test_oracle_matches_compiled_reference_random_masks(oracle):
     o = oracle.paged_attention(q, kc, vc, 0, gs, mask, 0.3)
     np.testing.assert_array_equal(o, r)
     assert not o[0, 2].any() and np.isfinite(o).all()
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+def test_oracle_scatter_matches_reference_index_put(oracle, dtype):
+    """reshape_and_cache as the reference writes it (manager.py:150-168):
+    cache[layer].view(-1, Hkv, D)[slot_mapping] = k, here with torch index_put on the same
+    arrays; bit-exact.  Slots past the pool (the reference would raise) and negative padding
+    slots (torch would wrap them) are skipped, and the oracle counts both."""
+    import torch
+    rng = np.random.default_rng(3)
+    L, NB, BS, H, D = 2, 9, 4, 3, 16
+    kc = rng.standard_normal((L, NB, BS, H, D)).astype(dtype)
+    vc = rng.standard_normal((L, NB, BS, H, D)).astype(dtype)
+    n = 20
+    slots = rng.permutation(NB * BS)[:n].astype(np.int64)
+    k = rng.standard_normal((n, H, D)).astype(dtype)
+    v = rng.standard_normal((n, H, D)).astype(dtype)
+    ref_k, ref_v = torch.from_numpy(kc.copy()), torch.from_numpy(vc.copy())
+    ref_k[1].view(-1, H, D)[torch.from_numpy(slots)] = torch.from_numpy(k)
+    ref_v[1].view(-1, H, D)[torch.from_numpy(slots)] = torch.from_numpy(v)
+    got_k, got_v = kc.copy(), vc.copy()
+    assert oracle.reshape_and_cache(k, v, got_k, got_v, slots, 1) == 0
+    np.testing.assert_array_equal(got_k, ref_k.numpy())
+    np.testing.assert_array_equal(got_v, ref_v.numpy())
+    # padding and out-of-range entries
+    bad = slots.copy()
+    bad[0], bad[1] = -1, NB * BS
+    got_k2, got_v2 = kc.copy(), vc.copy()
+    assert oracle.reshape_and_cache(k, v, got_k2, got_v2, bad, 1) == 2   # both skipped
+    keep = slice(2, None)
+    ref_k2 = torch.from_numpy(kc.copy())
+    ref_k2[1].view(-1, H, D)[torch.from_numpy(slots[keep])] = torch.from_numpy(k[keep])
+    np.testing.assert_array_equal(got_k2, ref_k2.numpy())
