@@ -172,7 +172,7 @@ def paged_ragged(q: np.ndarray, key_cache: np.ndarray, value_cache: np.ndarray, 
 def reshape_and_cache(key: np.ndarray, value: np.ndarray, key_cache: np.ndarray,
                       value_cache: np.ndarray, slot_mapping: np.ndarray, layer_idx: int) -> int:
     """In-place scatter of (Ntok,Hkv,D) rows into the caches (manager.py:150-168).  Returns the
-    number of out-of-range slots skipped."""
+    number of slots skipped: negative padding slots and slots past the pool."""
     assert key_cache.flags.c_contiguous and value_cache.flags.c_contiguous
     k = np.ascontiguousarray(key, dtype=key_cache.dtype)
     v = np.ascontiguousarray(value, dtype=value_cache.dtype)
