@@ -15,6 +15,7 @@ fixtures it wrote.
 """
 from __future__ import annotations
 
+import gzip
 import hashlib
 import json
 import os
@@ -152,10 +153,13 @@ def allocator_trace(out, seed=7, total_blocks=20, block_size=4, num_ops=400):
         "ops": ops}))
 
 
-def scheduler_trace(out, seed=11, total_blocks=40, block_size=4, num_requests=14):
-    """The reference Scheduler + LLMEngine (MockModelClient) on a pool small enough to force
-    recompute-preemption.  Records, per step, the allocator calls in order and every live
-    sequence's block table afterwards."""
+def record_schedule(seed, total_blocks, block_size, num_requests, max_batch_size=6,
+                    max_num_batched_tokens=64, max_model_len=200, max_prompt=24, max_out=20):
+    """The reference Scheduler + LLMEngine (MockModelClient) on one seeded request stream.
+    Returns (steps, finished): per step, the allocator calls in order, every live sequence's
+    block table afterwards, the free-block count and the preemption count; finished is False
+    when requests were still waiting after 400 steps (a prompt longer than the token budget is
+    never admitted, and the reference engine keeps stepping)."""
     rng = np.random.default_rng(seed)
     kv = PagedKVCacheManager(total_blocks=total_blocks, block_size=block_size, num_heads=2,
                              head_dim=8, num_layers=16, device="cpu")
@@ -178,14 +182,15 @@ def scheduler_trace(out, seed=11, total_blocks=40, block_size=4, num_requests=14
             calls.append(("free", seq.seq_id, 0))
 
     kv.allocate_prefix_blocks, kv.allocate_slot_for_next_token, kv.free_sequence = prefix, slot, free
-    sched = Scheduler(kv_cache_manager=kv, max_batch_size=6, max_num_batched_tokens=64,
-                      block_size=block_size, max_model_len=200)
+    sched = Scheduler(kv_cache_manager=kv, max_batch_size=max_batch_size,
+                      max_num_batched_tokens=max_num_batched_tokens, block_size=block_size,
+                      max_model_len=max_model_len)
     eng = LLMEngine(kv_cache_manager=kv, scheduler=sched, model_client=MockModelClient())
     seqs = []
     for _ in range(num_requests):
-        plen = int(rng.integers(1, 24))
+        plen = int(rng.integers(1, max_prompt))
         seqs.append(eng.add_request(prompt_token_ids=list(range(plen)),
-                                    max_tokens=int(rng.integers(2, 20))))
+                                    max_tokens=int(rng.integers(2, max_out))))
     steps = []
     for _ in range(400):
         if not eng.has_unfinished_requests():
@@ -197,8 +202,46 @@ def scheduler_trace(out, seed=11, total_blocks=40, block_size=4, num_requests=14
         steps.append({"calls": list(calls), "tables": live,
                       "free": kv.get_allocator().get_num_free_blocks(),
                       "preemptions": sched.preemption_count})
+    return steps, not eng.has_unfinished_requests()
+
+
+def scheduler_trace(out, seed=11, total_blocks=40, block_size=4, num_requests=14):
+    """One stream on a pool small enough to force recompute-preemption."""
+    steps, _ = record_schedule(seed, total_blocks, block_size, num_requests)
     out["sched_trace"] = np.asarray(json.dumps({
         "seed": seed, "total_blocks": total_blocks, "block_size": block_size, "steps": steps}))
+
+
+def scheduler_fuzz(num_streams=40, seed=2025):
+    """Many streams with random pool sizes, block sizes, batch and token budgets and request
+    mixes (tests/golden/sched_fuzz.json.gz): admission limits and recompute-preemption in many
+    combinations.  Each entry holds the parameters and the recorded steps."""
+    rng = np.random.default_rng(seed)
+    streams = []
+    while len(streams) < num_streams:
+        p = {"seed": int(rng.integers(0, 1 << 30)),
+             "block_size": int(rng.choice([1, 2, 4, 8, 16])),
+             "num_requests": int(rng.integers(1, 20)),
+             "max_batch_size": int(rng.integers(1, 10)),
+             "max_num_batched_tokens": int(rng.choice([16, 32, 64, 256])),
+             "max_prompt": int(rng.integers(2, 40)),
+             "max_out": int(rng.integers(3, 30))}
+        p["max_model_len"] = p["max_prompt"] + p["max_out"] + 8
+        # every request must fit the pool on its own (the scheduler rejects it otherwise)
+        need = -(-p["max_model_len"] // p["block_size"])
+        p["total_blocks"] = int(need + rng.integers(0, 3 * need))
+        try:
+            steps, finished = record_schedule(p["seed"], p["total_blocks"], p["block_size"],
+                                    p["num_requests"], p["max_batch_size"],
+                                    p["max_num_batched_tokens"], p["max_model_len"],
+                                    p["max_prompt"], p["max_out"])
+        except ValueError:
+            continue  # a request the reference refuses at add time (too long for the budget)
+        streams.append({"params": p, "steps": steps, "finished": finished})
+    path = os.path.join(HERE, "sched_fuzz.json.gz")
+    with gzip.open(path, "wt") as f:
+        json.dump(streams, f, separators=(",", ":"))
+    print("wrote", path, os.path.getsize(path), "bytes")
 
 
 def attention_cases(out):
@@ -295,4 +338,7 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["sched_fuzz"]:
+        scheduler_fuzz()
+    else:
+        main()
