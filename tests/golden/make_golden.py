@@ -103,6 +103,77 @@ def metadata_cases(out):
     out["meta_cases"] = np.asarray([c[0] for c in cases])
 
 
+def metadata_fuzz(num_cases=40, seed=77):
+    """PagedStepContext + build_block_tables on random steps (tests/golden/meta_fuzz.json.gz):
+    1-12 sequences with prompts of 1-40 tokens on a pool of block size 1-16 whose free list was
+    first shuffled by filler tables; each sequence is a whole-prompt prefill, a decode, or a chunk
+    of new tokens on its cached prompt.  Records the inputs (including the filler allocations and
+    the release order that shuffled the pool, and the prompt lengths, so the device pool can
+    replay the same allocation order) and every output."""
+    rng = np.random.default_rng(seed)
+    cases = []
+    for _ in range(num_cases):
+        bs = int(rng.choice([1, 2, 4, 8, 16]))
+        S = int(rng.integers(1, 13))
+        prompts = [int(x) for x in rng.integers(1, 41, size=S)]
+        kinds = [str(k) for k in rng.choice(["prefill", "decode", "chunk"], size=S)]
+        extra = [0 if k == "prefill" else (1 if k == "decode" else int(rng.integers(2, 20)))
+                 for k in kinds]
+        need = sum(-(-(p + e) // bs) for p, e in zip(prompts, extra))
+        total = need + int(rng.integers(0, need + 1))
+        store = PagedKVCacheManager(total_blocks=total, block_size=bs, num_heads=2, head_dim=8,
+                                    num_layers=1, device="cpu")
+        # shuffle the free list: filler tables take blocks, then give them back in random order
+        fillers = [int(x) for x in rng.integers(1, 3 * bs + 1, size=int(rng.integers(0, 4)))]
+        tabs = []
+        for n in fillers:
+            if -(-n // bs) > store.get_allocator().get_num_free_blocks():
+                break
+            t = llm_allocator_cpp.SequenceBlockTable(store.get_allocator())
+            for _ in range(n):
+                t.append_token()
+            tabs.append(t)
+        fillers = fillers[:len(tabs)]
+        release_order = [int(i) for i in rng.permutation(len(tabs))]
+        for i in release_order:
+            tabs[i].release()
+        seqs = []
+        for i, n in enumerate(prompts):
+            q = Sequence(seq_id=i + 1, prompt_token_ids=list(range(n)))
+            store.allocate_prefix_blocks(q)
+            seqs.append(q)
+        starts, counts = [], []
+        for q, k, e in zip(seqs, kinds, extra):
+            prev = q.block_table.get_tokens_count()
+            for _ in range(e):
+                store.allocate_slot_for_next_token(q)
+            if k == "prefill":
+                starts.append(0)
+                counts.append(prev)
+            else:
+                starts.append(prev if k == "chunk" else prev + e - 1)
+                counts.append(e)
+        ctx = PagedStepContext(store, seqs, starts, counts)
+        bt, cl = store.build_block_tables(seqs)
+        cases.append({
+            "block_size": bs, "total_blocks": total, "fillers": fillers,
+            "release_order": release_order, "prompts": prompts,
+            "tables": [list(map(int, q.block_table.get_physical_blocks())) for q in seqs],
+            "tokens": [int(q.block_table.get_tokens_count()) for q in seqs],
+            "starts": starts, "counts": counts,
+            "cu_seqlens": ctx.cu_seqlens.tolist(),
+            "cu_context_offsets": ctx.cu_context_offsets.tolist(),
+            "context_lens": [int(x) for x in ctx.context_lens],
+            "scatter_slots": ctx.scatter_slots.tolist(),
+            "gather_slots": ctx.gather_slots.tolist(),
+            "position_ids": ctx.position_ids(torch.device("cpu"))[0].tolist(),
+            "block_tables": bt.tolist(), "bt_context_lens": cl.tolist()})
+    path = os.path.join(HERE, "meta_fuzz.json.gz")
+    with gzip.open(path, "wt") as f:
+        json.dump(cases, f, separators=(",", ":"))
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
 def allocator_trace(out, seed=7, total_blocks=20, block_size=4, num_ops=400):
     """Seeded append/release/share/free ops on the reference PageAllocator/SequenceBlockTable.
     Records every op and the blocks each op handed out, so the FIFO order (including the order
@@ -340,5 +411,7 @@ def main():
 if __name__ == "__main__":
     if sys.argv[1:] == ["sched_fuzz"]:
         scheduler_fuzz()
+    elif sys.argv[1:] == ["meta_fuzz"]:
+        metadata_fuzz()
     else:
         main()

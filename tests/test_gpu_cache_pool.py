@@ -258,3 +258,43 @@ def test_step_metadata_stays_inside_its_outputs(bm):
     # a consistent call afterwards is clean
     _raw_metadata(pool, [0, 1], [19, 39], [1, 1], num_tokens=2, room=0, bt_stride=3)
     assert pool.status() == 0
+
+
+def test_step_metadata_matches_reference_fuzz(bm):
+    """The device pool and K4 on 40 random steps recorded from the reference (shuffled pools,
+    block sizes 1-16, mixed prefill / decode / chunk rows): the pool replays the reference's
+    allocation order (filler tables released in the recorded order, then the prompts, then the
+    step's new tokens) and K4's outputs equal the reference's."""
+    import gzip
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "meta_fuzz.json.gz")
+    with gzip.open(path, "rt") as f:
+        cases = json.load(f)
+    for i, c in enumerate(cases):
+        S, F, bs = len(c["prompts"]), len(c["fillers"]), c["block_size"]
+        width = max([len(t) for t in c["tables"]] + [-(-n // bs) for n in c["fillers"]] + [1])
+        pool = bm.DeviceBlockPool(c["total_blocks"], bs, S + F, width)
+        for k, n in enumerate(c["fillers"]):
+            pool.append_tokens(S + k, n)
+        pool.flush()
+        for k in c["release_order"]:
+            pool.release(S + k)
+        pool.flush()
+        for s, n in enumerate(c["prompts"]):
+            pool.append_tokens(s, n)
+        for s in range(S):
+            pool.append_tokens(s, c["tokens"][s] - c["prompts"][s])
+        pool.flush()
+        assert [pool.table(s) for s in range(S)] == c["tables"], i
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
+        md = pool.build_step_metadata(
+            torch.arange(S, dtype=torch.int32, device="cuda"), i32(c["starts"]), i32(c["counts"]),
+            sum(c["counts"]), bt_stride=len(c["block_tables"][0]), with_gather_slots=True,
+            num_context_tokens=sum(c["context_lens"]))
+        for key in ("cu_seqlens", "cu_context_offsets", "context_lens", "gather_slots",
+                    "block_tables"):
+            assert md[key].cpu().tolist() == c[key], (i, key)
+        assert md["slot_mapping"].cpu().tolist() == c["scatter_slots"], i
+        assert md["position_ids"].cpu().tolist() == c["position_ids"], i
+        assert pool.status() == 0, i

@@ -242,3 +242,25 @@ def test_oracle_scatter_matches_reference_index_put(oracle, dtype):
     ref_k2 = torch.from_numpy(kc.copy())
     ref_k2[1].view(-1, H, D)[torch.from_numpy(slots[keep])] = torch.from_numpy(k[keep])
     np.testing.assert_array_equal(got_k2, ref_k2.numpy())
+
+
+def test_metadata_matches_reference_fuzz(oracle):
+    """40 random steps recorded from the reference's PagedStepContext + build_block_tables
+    (tests/golden/meta_fuzz.json.gz): mixed prefill / decode / chunk rows, block sizes 1-16,
+    shuffled pools."""
+    import gzip
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "meta_fuzz.json.gz")
+    with gzip.open(path, "rt") as f:
+        cases = json.load(f)
+    assert len(cases) == 40
+    for i, c in enumerate(cases):
+        md = oracle.step_metadata(c["tables"], c["tokens"], c["starts"], c["counts"],
+                                  c["block_size"])
+        for key in ("cu_seqlens", "cu_context_offsets", "context_lens", "scatter_slots",
+                    "gather_slots"):
+            assert md[key].tolist() == c[key], (i, key)
+        assert md["position_ids"][0].tolist() == c["position_ids"], i
+        bt, cl = oracle.build_block_tables(c["tables"], c["tokens"])
+        assert bt.tolist() == c["block_tables"] and cl.tolist() == c["bt_context_lens"], i
