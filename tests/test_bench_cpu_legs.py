@@ -58,3 +58,21 @@ def test_config4_request_stream_is_the_seeded_one(pkg):
     assert [len(p) for p in prompts] == plens[:5].astype(int).tolist()
     assert prompts[0] == rng.integers(0, 32000, size=int(plens[0])).tolist()
     assert 64 <= olens.min() and olens.max() <= 512 and max(map(max, prompts)) < 32000
+
+
+def test_roofline_arithmetic_matches_the_quoted_figures(pkg):
+    """The algorithmic bytes and flops the bench divides by measured time are the figures the
+    profile summaries quote: config-2 decode 1,421,076,360 B per launch (K and V of every context
+    token once per KV head, Q, O, block ids, lengths), config-3 prefill chunks 533,616,574,464
+    flop (QK^T and PV over the causal region only)."""
+    b2 = pkg.workloads.config2(seed=0)
+    step, decode = bench.step_bytes(b2)
+    assert int(b2.context_lens.sum()) == 345897
+    assert decode == 1421076360
+    assert step - decode == 256 * 8 * 128 * 2 * 2 * 2 + 256 * 8   # new K/V rows read + written, slots
+    full = pkg.workloads.config3(seed=0)
+    pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:16],
+                               new_token_counts=full.new_token_counts[:16], num_query_heads=32,
+                               num_kv_heads=8, head_dim=128, block_size=16)
+    assert pre.num_tokens == 17543
+    assert bench.attention_flops(pre) == 533616574464
