@@ -137,8 +137,9 @@ int b200_paged_decode(const B200DecodeParams* p, void* workspace, size_t workspa
  * synchronisation): the scratch comes from a static device array of
  * B200_DECODE_STATIC_SCRATCH_BYTES that every GPU loading this library holds until exit.  Batches
  * needing more scratch than that (b200_paged_decode_workspace_bytes) are rejected with
- * B200_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's device address
- * (make it before any stream capture).  Calls share the array: each call resets what must start at
+ * B200_ERR_INVALID_ARGUMENT.  The first call in a device's CUDA context looks up the array's
+ * device address (make it before any stream capture); after a cudaDeviceReset the next call looks
+ * it up again in the new context.  Calls share the array: each call resets what must start at
  * zero, and calls that overlap on the GPU race.  Allocates nothing. */
 #define B200_DECODE_STATIC_SCRATCH_BYTES ((size_t)64 << 20)
 int b200_paged_decode_static(const B200DecodeParams* p, void* stream);
