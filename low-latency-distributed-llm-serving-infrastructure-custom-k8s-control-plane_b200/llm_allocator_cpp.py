@@ -174,7 +174,15 @@ class SequenceBlockTable:
 
 def paged_attention(query, key_cache, value_cache, layer_idx, gather_slots, attention_mask,
                     scaling):
-    """The reference binding's contract (bindings.cpp:10-76) on the B200 kernel."""
+    """The reference binding's contract (csrc/src/bindings.cpp:10-76) on the B200 kernel.
+
+    Inputs may be numpy arrays or torch tensors, on the host or on the GPU; host inputs are
+    force-cast to the binding's types (fp32, int32 slots, uint8 mask) and copied to the device.
+    Device caches must already be fp32, the only cache type the reference kernel takes: the
+    whole cache is never converted on the device.  Returns a numpy array (1, Nq, Hq, D) fp32,
+    as the binding does, so the reference's unchanged caller
+    (app/model/attention_backends.py:108-117, ``torch.from_numpy(output)``) works as is.  The
+    device-tensor form that returns a CUDA tensor is ``paged_ops.paged_attention_masked``."""
     import numpy as np
     import torch
 
@@ -182,15 +190,19 @@ def paged_attention(query, key_cache, value_cache, layer_idx, gather_slots, atte
 
     if not torch.cuda.is_available():
         raise RuntimeError("paged_attention runs on the GPU; no CUDA device is available")
+    types = (np.float32, np.float32, np.float32, np.int32, np.uint8)
     args = [query, key_cache, value_cache, gather_slots, attention_mask]
-    on_device = all(isinstance(a, torch.Tensor) and a.is_cuda for a in args)
     dev = next((a.device for a in args if isinstance(a, torch.Tensor) and a.is_cuda),
-               torch.device("cuda"))
-    t = [a.to(dev) if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-         for a in args]
+               torch.device("cuda", torch.cuda.current_device()))
+    t = []
+    for a, ty in zip(args, types):
+        if isinstance(a, torch.Tensor) and a.is_cuda:
+            t.append(a.to(dev))
+            continue
+        if isinstance(a, torch.Tensor):
+            a = a.detach().numpy() if a.dtype != torch.bfloat16 else a.detach().float().numpy()
+        t.append(torch.from_numpy(np.ascontiguousarray(a, dtype=ty)).to(dev))
     out = paged_attention_masked(t[0], t[1], t[2], int(layer_idx), t[3], t[4], float(scaling))
-    if on_device:
-        return out
     return out.cpu().numpy()
 
 

@@ -312,9 +312,12 @@ def copy_blocks(src_key_cache: torch.Tensor, src_value_cache: Optional[torch.Ten
 def paged_attention_masked(query: torch.Tensor, key_cache: torch.Tensor,
                            value_cache: torch.Tensor, layer_idx: int, gather_slots: torch.Tensor,
                            attention_mask: torch.Tensor, scaling: float) -> torch.Tensor:
-    """The reference kernel's own contract (csrc/src/bindings.cpp:10-76) on the device:
-    query (1,Hq,Nq,D) fp32, caches fp32, gather_slots (Nctx,) int32, mask (1,1,Nq,Nctx)
-    -> (1,Nq,Hq,D) fp32, through the C symbol `paged_attention`."""
+    """The reference kernel's contract (csrc/src/bindings.cpp:10-76) on device tensors:
+    query (1,Hq,Nq,D), fp32 caches (L,NB,BS,Hkv,D), gather_slots (Nctx,), mask (1,1,Nq,Nctx)
+    -> (1,Nq,Hq,D) fp32 on the device.  Runs ``b200_paged_attention``, the status-returning form
+    of the C symbol ``paged_attention`` (same kernel, same arguments).  The caches must be fp32,
+    as in the reference; they are never converted here (a whole-cache copy per layer per call
+    would cost far more than the attention).  The query is cast to fp32 if it is not already."""
     _require_cuda(query, key_cache, value_cache, gather_slots, attention_mask)
     if query.dim() != 4:
         raise RuntimeError("query must be 4-D (1, heads, seq, dim)")
@@ -324,9 +327,15 @@ def paged_attention_masked(query: torch.Tensor, key_cache: torch.Tensor,
         raise RuntimeError("gather_slots must be 1-D")
     if attention_mask.dim() != 4:
         raise RuntimeError("attention_mask must be 4-D (1, 1, query, context)")
+    for name, c in (("key_cache", key_cache), ("value_cache", value_cache)):
+        if c.dtype != torch.float32:
+            raise TypeError(f"{name} must be float32 (the reference kernel's cache type), got "
+                            f"{c.dtype}; the bf16/f16 paths are paged_decode / paged_prefill")
+    if value_cache.shape != key_cache.shape:
+        raise RuntimeError("key_cache and value_cache must have the same shape")
     q = query.to(torch.float32).contiguous()
-    kc = key_cache.to(torch.float32).contiguous()
-    vc = value_cache.to(torch.float32).contiguous()
+    kc = key_cache.contiguous()
+    vc = value_cache.contiguous()
     gs = gather_slots.to(torch.int32).contiguous()
     m = attention_mask.to(torch.uint8).contiguous()
     dims = N.PagedAttentionDims(q.shape[1], q.shape[2], q.shape[3], kc.shape[0], kc.shape[1],

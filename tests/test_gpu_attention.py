@@ -22,7 +22,8 @@ def ops(pkg):
 
 
 def test_reference_signature_config1(golden, ops):
-    """Config 1 through the C symbol `paged_attention` (same contract as the reference's)."""
+    """Config 1 through b200_paged_attention, the status-returning form of the reference-signature
+    symbol (the void symbol itself: tests/test_gpu_reference_binding.py)."""
     from config1_inputs import config1_inputs
     b, q, kc, vc, gs, mask = config1_inputs()
     dev = torch.device("cuda")
