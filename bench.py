@@ -1,19 +1,30 @@
-"""Benchmark of the paged-attention decode hot path on B200.
+"""Benchmark of the paged-attention hot path on B200.
 
-One step = reshape_and_cache of each sequence's new token + paged-attention decode over the
-whole batch (256 sequences, lognormal contexts median 1024 clipped to [16, 4096], GQA 32/8,
-head_dim 128, block size 16, bf16, shuffled block pool), one layer.
+Headline (`value`): one step = reshape_and_cache of each sequence's new token
++ paged-attention decode over the whole batch (256 sequences, lognormal contexts median 1024
+clipped to [16, 4096], GQA 32/8, head_dim 128, block size 16, bf16, shuffled block pool), one
+layer.  Metric: algorithmic HBM GB/s of the step (bytes every step must move: each context
+token's K and V once per KV head, queries, outputs, block tables, lengths, the new K/V rows and
+slots).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own independent config-2 batch (the
-path partitions by sequence; no data-path collective), so scaling is weak and `value` is the sum
-of all ranks' bytes over the max-over-ranks time.  The reference arm (`--impl reference`) times
-the reference's own CPU kernel (oracle/_ref, compiled from the reference's sources; the oracle's
-C restatement when that build is absent) on the host cores, rank 0 only.
+The same default run then adds two more legs to its JSON line:
+  * `engine` -- the north star's engine target: the 8B-shape engine,
+    tensor-parallel by KV head over the launched ranks (NCCL all-reduce after o_proj and
+    down_proj), with its block pool at 95 % occupancy and a queue of long prompts, so the
+    reference's recompute-preemption policy runs; output tokens/s over `--engine-steps` steps
+    (max over ranks).  Under TP it also carries `tp_parity`: greedy tokens of a small fp32 model
+    at TP N against the same engine on one GPU.
+  * `prefill` (one GPU) -- the tcgen05 prefill kernel alone on the config-3 prefill chunks,
+    TFLOP/s against the measured dense bf16 peak.
 
-Metric: algorithmic HBM GB/s of the step (bytes every step must move: each context token's K and
-V once per KV head, queries, outputs, block tables, lengths, the new K/V rows and slots).
+Multi-GPU (torchrun, one rank per GPU): for the headline, every rank runs its own independent
+config-2 batch (the path partitions by sequence; no data-path collective), so scaling is weak and
+`value` is the sum of all ranks' bytes over the max-over-ranks time.  The reference arm
+(`--impl reference`) times the reference's own CPU kernel (oracle/_ref, compiled from the
+reference's sources; the oracle's C restatement when that build is absent) on the host cores,
+rank 0 only.
 """
 from __future__ import annotations
 
@@ -418,10 +429,32 @@ def ours_arm(args):
                          f"{int(b.context_lens[:args.cpu_seqs].sum())}), one call per sequence, "
                          f"bf16 values upcast to fp32; {passes} passes, {passes * dt:.1f} s"}
 
+    # The north star's engine target (config 5, TP by KV head over these ranks, preemption
+    # forced) and, under TP, the token check against one GPU; then the prefill kernel (rank 0).
+    del kc, vc, bufs, h_in, h_out
+    torch.cuda.empty_cache()
+    engine = None
+    tp_tokens = None
+    if not args.no_engine:
+        engine = run_engine5(args, world, rank, dev, args.engine_steps, 3, sample_clocks=True)
+        if world > 1:
+            tp_tokens = tp_parity_tokens(world, rank, dev)
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    if tp_tokens is not None:
+        ref_tokens = tp_parity_tokens(1, 0, dev)
+        engine["tp_parity"] = {
+            "match": tp_tokens[0] == ref_tokens[0],
+            "check": f"greedy tokens of a 2-layer fp32 random-init Llama (hidden 256, 16/8 "
+                     f"heads) on 4 prompts x 12 tokens at TP{world} (graph steps "
+                     f"{tp_tokens[1]}) vs the same engine on one GPU, run by rank 0 after the "
+                     f"process group is torn down"}
+    elif engine is not None:
+        engine["tp_parity"] = None
+    prefill = prefill_measure(dev, 20, 3) if world == 1 and not args.no_prefill else None
     peak, peak_kind = load_peaks()
     ms_per_step = elapsed_ms / args.steps
     value = world * total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -455,6 +488,10 @@ def ours_arm(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if engine is not None:
+        line["engine"] = engine
+    if prefill is not None:
+        line["prefill"] = prefill
     print(json.dumps(line))
     return 0
 
@@ -660,20 +697,33 @@ def engine4_arm(args):
     return 0
 
 
-def engine5_arm(args):
-    """random-init Llama-3-8B shape (32 x 4096, 32/8 heads, D 128, FFN 14336,
-    vocab 128256, bf16), tensor-parallel by KV head over the launched ranks.  Long contexts
-    U[8192, 32768] are placed in the cache (K/V filled with random values, blocks handed out by
-    the device pool from a shuffled free list) so that they occupy 95 % of a pool of `--kv-gb`
-    per GPU; then `--steps` engine decode steps run under the continuous-batching scheduler
-    (preemption/recompute if the pool runs dry).  Value: output tokens/s (max over ranks)."""
+ENGINE5_MAX_OUT = 1024
+ENGINE5_MAX_LEN = 32768 + ENGINE5_MAX_OUT
+
+
+def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
+    """BASELINE config 5 under preemption pressure, tensor-parallel by KV head over the launched
+    ranks (call on every rank, inside the process group when world > 1).
+
+    Random-init Llama-3-8B shape (32 x 4096, 32/8 heads, D 128, FFN 14336, vocab 128256, bf16).
+    Running sequences with contexts U[8192, 32768] are placed in the cache (random K/V, blocks
+    handed out by the device pool from a shuffled free list) until they hold 95 % of a pool of
+    `--kv-gb` per GPU; behind them waits a queue of half as many requests with prompts
+    U[8192, 32768] of uniform-random token ids.  Outputs are U[256, 1024] tokens.  The reference
+    scheduling policy then runs (scheduler.py:84-151): waiting requests are admitted whenever
+    their whole prompt fits, which drives the pool to full, and a running sequence that needs a
+    block when none is free is preempted -- its blocks freed, itself re-queued at the front and
+    later recomputed from its prompt and outputs.  The per-step token budget is
+    `ENGINE5_MAX_LEN * world`, so every TP size admits the same work per rank (weak scaling: TP t
+    holds t times the sequences in the same bytes per GPU).
+
+    Returns a dict (identical on every rank; times are the max over ranks)."""
     import torch
     import torch.distributed as dist
     import __graft_entry__
-    pkg = __graft_entry__.load_package()
-    from llm_serving_b200.engine import build_engine, Sequence, SequenceStatus
+    __graft_entry__.load_package()
+    from llm_serving_b200.engine import build_engine, SequenceStatus
     from llm_serving_b200.model import CONFIG5, kv_bytes_per_token
-    world, rank, dev = _dist_setup()
     shape = CONFIG5
     bs = 16
     blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(shape, world) * bs))
@@ -687,9 +737,14 @@ def engine5_arm(args):
             break
         ctxs.append(c)
         used += need
+    out_lens = rng.integers(256, ENGINE5_MAX_OUT + 1, size=len(ctxs))
+    n_wait = len(ctxs) // 2
+    wait_lens = rng.integers(8192, 32769, size=n_wait)
+    wait_outs = rng.integers(256, ENGINE5_MAX_OUT + 1, size=n_wait)
     eng = build_engine(shape, total_blocks=blocks, block_size=bs, rank=rank, world=world,
-                       device=dev, seed=0, max_batch_size=max(256, len(ctxs)),
-                       max_num_batched_tokens=40000, max_model_len=32768 + 1024)
+                       device=dev, seed=0, max_batch_size=32 * world,
+                       max_num_batched_tokens=ENGINE5_MAX_LEN * world,
+                       max_model_len=ENGINE5_MAX_LEN)
     kv, pool = eng.kv, eng.kv.pool
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
@@ -706,58 +761,176 @@ def engine5_arm(args):
     for f in rng.permutation(fillers):
         pool.release(base_slot + int(f))
     pool.flush()
-    seqs = []
-    for c in ctxs:
-        s = eng.add_request([1] * c, max_tokens=args.steps + 8)
+    for c, o in zip(ctxs, out_lens):
+        s = eng.add_request([1] * c, max_tokens=int(o))
         eng.scheduler.waiting.remove(s)
         kv.allocate_prefix_blocks(s)
         s.output_token_ids.append(2)          # as if prefilled: the next step decodes
         s.status = SequenceStatus.RUNNING
         eng.scheduler.running.append(s)
-        seqs.append(s)
-    # the cache holds random K/V for every allocated token (no prefill pass: decode is measured)
+    # the cache holds random K/V for every allocated token (no prefill pass for these)
     pool.flush()
-    for _ in range(max(args.warmup, 2)):
+    for c, o in zip(wait_lens, wait_outs):
+        eng.add_request(rng.integers(0, shape.vocab, size=int(c)).tolist(), max_tokens=int(o))
+    for _ in range(max(warmup, 3)):
         eng.step()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
+    pre0 = eng.scheduler.preemption_count
+    gen0, ptok0, steps0, gsteps0 = (eng.tokens_generated, eng.prefill_tokens, eng.steps,
+                                    eng.graph_steps)
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) if sample_clocks else None
+    if sampler:
+        sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gen0 = eng.tokens_generated
     e0.record()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         eng.step()
     e1.record()
     torch.cuda.synchronize(dev)
     wall = time.perf_counter() - t0
+    clocks = sampler.stop() if sampler else None
     ms = e0.elapsed_time(e1)
-    toks = eng.tokens_generated - gen0
-    tt = torch.tensor([ms], dtype=torch.float64, device=dev)
-    graph_steps = eng.graph_steps
+    tt = torch.tensor([ms, wall * 1e3], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms, wall_ms = tt.tolist()
+    toks = eng.tokens_generated - gen0
+    res = {
+        "tokens_per_s": round(toks / (ms * 1e-3), 1), "tp": world, "steps": steps,
+        "ms_per_step": round(ms / steps, 3), "output_tokens": toks,
+        "prefill_tokens": eng.prefill_tokens - ptok0,
+        "preemptions": eng.scheduler.preemption_count - pre0,
+        "preemptions_incl_warmup": eng.scheduler.preemption_count,
+        "graph_steps": eng.graph_steps - gsteps0, "eager_steps": steps - (eng.graph_steps - gsteps0),
+        "sequences": len(ctxs), "waiting_at_start": n_wait,
+        "running_at_end": len(eng.scheduler.running), "waiting_at_end": len(eng.scheduler.waiting),
+        "sum_ctx": int(sum(ctxs)), "kv_pool_blocks_per_gpu": blocks, "kv_gb_per_gpu": args.kv_gb,
+        "wall_ms_max_over_ranks": round(wall_ms, 1),
+        "workload": "config5: Llama-3-8B shape random init, bf16, TP by KV head; running "
+                    "contexts U[8192,32768] at 95% pool occupancy (shuffled free list) + a queue "
+                    "of half as many prompts U[8192,32768]; outputs U[256,1024]; reference "
+                    "admission and recompute-preemption policy; weak scaling (pool bytes per GPU "
+                    "fixed, TP t holds t x the sequences)",
+        "device_status": eng.kv.pool.status(),
+    }
+    if clocks is not None:
+        res["clocks"] = clocks
     eng.release_graphs()  # captured graphs hold NCCL calls: release before the process group
+    del eng, kv, pool
+    torch.cuda.empty_cache()
+    return res
+
+
+TP_PARITY_SHAPE = dict(num_layers=2, hidden=256, num_heads=16, num_kv_heads=8, head_dim=32,
+                       ffn=512, vocab=400)
+
+
+def tp_parity_tokens(world, rank, dev):
+    """Greedy tokens of a small fp32 random-init Llama (weights drawn whole from one seed, so every
+    world size holds the same model) on 4 prompts, through the engine at tensor-parallel size
+    `world` (inside the process group when world > 1): decode steps as captured graphs holding
+    the all-reduces, prefill eager."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from llm_serving_b200.engine import build_engine
+    from llm_serving_b200.model import LlamaShape
+    shape = LlamaShape(**TP_PARITY_SHAPE)
+    eng = build_engine(shape, total_blocks=128, block_size=16, rank=rank, world=world, device=dev,
+                       dtype=torch.float32, seed=3, max_batch_size=8, max_model_len=256,
+                       full_init=True)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, shape.vocab, (int(n),), generator=g).tolist()
+               for n in (3, 30, 17, 64)]
+    seqs = [eng.add_request(p, max_tokens=12) for p in prompts]
+    while eng.has_unfinished_requests():
+        eng.step()
+    toks = [s.output_token_ids for s in seqs]
+    graphs = eng.graph_steps
+    eng.release_graphs()
+    del eng
+    return toks, graphs
+
+
+def engine5_arm(args):
+    """`--workload engine5`: the config-5 engine alone (see run_engine5), one JSON line."""
+    import torch.distributed as dist
+    world, rank, dev = _dist_setup()
+    res = run_engine5(args, world, rank, dev, args.steps, args.warmup, sample_clocks=True)
     if world > 1:
         dist.destroy_process_group()
-    ms = float(tt.item())
     if rank != 0:
         return 0
     line = {
-        "metric": "engine output tokens/s (config 5, decode at long context)",
-        "value": round(toks / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "metric": "engine output tokens/s (config 5, long context under preemption)",
+        "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config5: Llama-3-8B shape random init, contexts U[8192,32768] at "
-                               "95% pool occupancy (shuffled free list), decode steps",
-                   "parallelism": f"tp{world} (KV heads)", "sequences": len(ctxs),
-                   "sum_ctx": int(sum(ctxs)), "kv_pool_blocks_per_gpu": blocks,
-                   "kv_gb_per_gpu": args.kv_gb},
-        "preemptions": eng.scheduler.preemption_count, "graph_steps": graph_steps,
-        "wall_s": round(wall, 3),
+        "config": {"workload": res["workload"], "parallelism": f"tp{world} (KV heads)"},
+        "engine": res,
     }
     print(json.dumps(line))
     return 0
+
+
+def prefill_measure(dev, steps, warmup):
+    """K3 alone on the 16 prefill chunks of the config-3 step (lengths U[128,2048] on prior
+    contexts U[0,2048], GQA 32/8, D 128, bf16): CUDA-event time of the paged_prefill call and
+    its causal QK^T + PV flops against the measured dense bf16 peak."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200 import paged_ops
+    full = pkg.workloads.config3(seed=0)
+    npre = 16
+    pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
+                               new_token_counts=full.new_token_counts[:npre], num_query_heads=32,
+                               num_kv_heads=8, head_dim=128, block_size=16)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    shape = (1, pre.total_blocks, pre.block_size, pre.num_kv_heads, pre.head_dim)
+    kc = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn((pre.num_tokens, pre.num_query_heads, pre.head_dim), generator=g,
+                    device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    bt = torch.from_numpy(pre.block_tables()).to(dev)
+    cu = torch.from_numpy(pre.cu_seqlens()).to(dev)
+    ctx = torch.from_numpy(pre.context_lens.astype(np.int32)).to(dev)
+    mq, mc = int(pre.new_token_counts.max()), int(pre.context_lens.max())
+
+    def call():
+        paged_ops.paged_prefill(q, kc, vc, 0, bt, cu, ctx, pre.scale, mq, mc, out=out)
+
+    for _ in range(max(warmup, 3)):
+        call()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    flops = attention_flops(pre)
+    peak, src = 1590.0, "fallback"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        pass
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "b200_paged_prefill (prefill_tc_kernel, tcgen05)",
+            "workload": "the 16 prefill chunks of the config-3 step (%d new tokens)"
+                        % pre.num_tokens,
+            "ms": round(ms, 4), "flops": flops, "tflops": round(tflops, 2),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
+                         "peak_source": src + " (burst bf16 GEMM)"}}
 
 
 def swap_arm(args):
@@ -969,6 +1142,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="minimum CPU work of the cpu_baseline leg (passes over the sample)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-engine", action="store_true",
+                    help="skip the config-5 engine leg of the default run")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the prefill-kernel leg of the default run")
+    ap.add_argument("--engine-steps", type=int, default=600,
+                    help="timed engine steps of the config-5 leg of the default run")
     ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
                                            "meta"],
                     default="config2")

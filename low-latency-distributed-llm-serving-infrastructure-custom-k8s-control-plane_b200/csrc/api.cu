@@ -10,6 +10,7 @@
 
 #include "attention.cuh"
 #include "cache_ops.cuh"
+#include "nvtx.cuh"
 
 namespace {
 
@@ -241,6 +242,7 @@ int b200_paged_attention(const float* query, const float* key_cache, const float
                          int32_t layer_idx, PagedAttentionDims dims, const int32_t* gather_slots,
                          const uint8_t* attention_mask, float scaling, float* output,
                          int32_t* status_word, void* stream) {
+  b200::NvtxRange nvtx_range("b200_paged_attention");
   B200CacheGeometry g{dims.num_layers, dims.total_blocks, dims.block_size, dims.num_kv_heads,
                       dims.head_dim, B200_DTYPE_F32};
   int rc = validate_geom(g, layer_idx, dims.num_query_heads);
@@ -419,6 +421,7 @@ extern "C" {
 
 int b200_paged_decode(const B200DecodeParams* pp, void* workspace, size_t workspace_bytes,
                       void* stream) {
+  b200::NvtxRange nvtx_range("b200_paged_decode");
   if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
   const B200DecodeParams& p = *pp;
   int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
@@ -518,6 +521,7 @@ size_t b200_paged_prefill_workspace_bytes(const B200PrefillParams* p) {
 
 int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t workspace_bytes,
                        void* stream) {
+  b200::NvtxRange nvtx_range("b200_paged_prefill");
   if (pp == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null params");
   const B200PrefillParams& p = *pp;
   int rc = validate_geom(p.geom, p.layer_idx, p.num_query_heads);
@@ -631,6 +635,7 @@ int b200_reshape_and_cache(const void* key, int64_t k_stride_token, int64_t k_st
                            void* key_cache, void* value_cache, const B200CacheGeometry* geom,
                            int32_t layer_idx, const int64_t* slot_mapping, int32_t num_tokens,
                            int32_t* status_word, void* stream) {
+  b200::NvtxRange nvtx_range("b200_reshape_and_cache");
   if (geom == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null geometry");
   const B200CacheGeometry& g = *geom;
   const int es = esize_of(g.dtype);
@@ -678,6 +683,7 @@ int b200_rope_reshape_and_cache(const void* qkv, int64_t qkv_stride_token, int32
                                 void* key_cache, void* value_cache, const B200CacheGeometry* geom,
                                 int32_t layer_idx, const int64_t* slot_mapping,
                                 int32_t* status_word, void* stream) {
+  b200::NvtxRange nvtx_range("b200_rope_reshape_and_cache");
   if (geom == nullptr) return fail(B200_ERR_INVALID_ARGUMENT, "null geometry");
   const B200CacheGeometry& g = *geom;
   if (esize_of(g.dtype) == 0) return fail(B200_ERR_UNSUPPORTED, "unsupported dtype");
@@ -753,6 +759,7 @@ int b200_copy_blocks(const void* src_key_cache, const void* src_value_cache,
                      void* dst_value_cache, const B200CacheGeometry* dst_geom,
                      const int32_t* src_blocks, const int32_t* dst_blocks, int32_t num_blocks,
                      int32_t* status_word, void* stream) {
+  b200::NvtxRange nvtx_range("b200_copy_blocks");
   if (src_geom == nullptr || dst_geom == nullptr)
     return fail(B200_ERR_INVALID_ARGUMENT, "null geometry");
   const B200CacheGeometry& s = *src_geom;

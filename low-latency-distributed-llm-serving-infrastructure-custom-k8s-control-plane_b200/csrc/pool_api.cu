@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "cache_ops.cuh"
+#include "nvtx.cuh"
 
 namespace {
 int pfail(int code, const char* msg) {
@@ -262,6 +263,7 @@ int32_t b200_pool_cow_pairs(const B200BlockPool* p, const int32_t** old_blocks,
 }
 
 int b200_pool_flush(B200BlockPool* p, void* stream) {
+  b200::NvtxRange nvtx_range("b200_pool_flush");
   if (p == nullptr) return pfail(B200_ERR_INVALID_ARGUMENT, "null pool");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   p->cow_count = 0;
@@ -330,6 +332,7 @@ int b200_build_step_metadata(const B200BlockPool* pool, const int32_t* seq_slots
                              int64_t* cu_context, int32_t* context_lens, int64_t* position_ids,
                              int64_t* slot_mapping, int32_t* block_tables, int32_t bt_stride,
                              int64_t* gather_slots, int64_t num_context_tokens, void* stream) {
+  b200::NvtxRange nvtx_range("b200_build_step_metadata");
   if (pool == nullptr) return pfail(B200_ERR_INVALID_ARGUMENT, "null pool");
   if (num_seqs < 0 || num_tokens < 0 || bt_stride < 0 || num_context_tokens < 0)
     return pfail(B200_ERR_INVALID_ARGUMENT, "negative sizes");

@@ -244,15 +244,33 @@ class Engine:
         self._graph_ws = None
 
     def step(self) -> Dict[str, List[Sequence]]:
+        """One continuous-batching step.  NVTX ranges mark its phases on a timeline profile:
+        ``engine.step`` around it, ``schedule``, then ``decode_graph`` (replay of a captured
+        decode step) or ``eager_step`` (prefill or mixed batch); the C library adds one range per
+        kernel-launching call inside them."""
+        nvtx = torch.cuda.nvtx
+        nvtx.range_push("engine.step")
+        try:
+            return self._step(nvtx)
+        finally:
+            nvtx.range_pop()
+
+    def _step(self, nvtx) -> Dict[str, List[Sequence]]:
+        nvtx.range_push("schedule")
         out = self.scheduler.schedule()
+        nvtx.range_pop()
         seqs = out.scheduled_prefills + out.scheduled_decodes
         if not seqs:
             return {"finished": [], "running": []}
         next_tokens = None
         if self.cuda_graphs and not out.scheduled_prefills:
+            nvtx.range_push("decode_graph")
             next_tokens = self._graph_decode(out.scheduled_decodes)
+            nvtx.range_pop()
         if next_tokens is None:
+            nvtx.range_push("eager_step")
             next_tokens = self._eager_step(out)
+            nvtx.range_pop()
         now = time.perf_counter()
         for s, t in zip(seqs, next_tokens):
             if s.first_token_time is None:
