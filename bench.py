@@ -708,7 +708,7 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
     Random-init Llama-3-8B shape (32 x 4096, 32/8 heads, D 128, FFN 14336, vocab 128256, bf16).
     Running sequences with contexts U[8192, 32768] are placed in the cache (random K/V, blocks
     handed out by the device pool from a shuffled free list) until they hold 95 % of a pool of
-    `--kv-gb` per GPU; behind them waits a queue of half as many requests with prompts
+    `--kv-gb` per GPU; behind them waits a queue of twice as many requests with prompts
     U[8192, 32768] of uniform-random token ids.  Outputs are U[256, 1024] tokens.  The reference
     scheduling policy then runs (scheduler.py:84-151): waiting requests are admitted whenever
     their whole prompt fits, which drives the pool to full, and a running sequence that needs a
@@ -738,7 +738,7 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
         ctxs.append(c)
         used += need
     out_lens = rng.integers(256, ENGINE5_MAX_OUT + 1, size=len(ctxs))
-    n_wait = len(ctxs) // 2
+    n_wait = 2 * len(ctxs)
     wait_lens = rng.integers(8192, 32769, size=n_wait)
     wait_outs = rng.integers(256, ENGINE5_MAX_OUT + 1, size=n_wait)
     eng = build_engine(shape, total_blocks=blocks, block_size=bs, rank=rank, world=world,
@@ -802,6 +802,7 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
         "tokens_per_s": round(toks / (ms * 1e-3), 1), "tp": world, "steps": steps,
         "ms_per_step": round(ms / steps, 3), "output_tokens": toks,
         "prefill_tokens": eng.prefill_tokens - ptok0,
+        "processed_tokens_per_s": round((toks + eng.prefill_tokens - ptok0) / (ms * 1e-3), 1),
         "preemptions": eng.scheduler.preemption_count - pre0,
         "preemptions_incl_warmup": eng.scheduler.preemption_count,
         "graph_steps": eng.graph_steps - gsteps0, "eager_steps": steps - (eng.graph_steps - gsteps0),
@@ -811,7 +812,7 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
         "wall_ms_max_over_ranks": round(wall_ms, 1),
         "workload": "config5: Llama-3-8B shape random init, bf16, TP by KV head; running "
                     "contexts U[8192,32768] at 95% pool occupancy (shuffled free list) + a queue "
-                    "of half as many prompts U[8192,32768]; outputs U[256,1024]; reference "
+                    "of twice as many prompts U[8192,32768]; outputs U[256,1024]; reference "
                     "admission and recompute-preemption policy; weak scaling (pool bytes per GPU "
                     "fixed, TP t holds t x the sequences)",
         "device_status": eng.kv.pool.status(),
