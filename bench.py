@@ -478,6 +478,7 @@ def config3_arm(args):
     from llm_serving_b200 import paged_ops
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    pkg._native.lib().b200_set_prefill_two_tiles(1 if args.prefill_two_tiles else 0)
     full = pkg.workloads.config3(seed=0)
     npre = 16
     pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
@@ -546,6 +547,7 @@ def config3_arm(args):
                                       "peak": peak, "unit": "TFLOP/s",
                                       "frac": round(tflops / peak, 4)}},
         "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
+        "prefill_kernel": "two query tiles per item" if args.prefill_two_tiles else "one query tile per item",
         "device_status": paged_ops.read_status(dev),
     }
     if not args.no_cpu:
@@ -969,6 +971,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="minimum CPU work of the cpu_baseline leg (passes over the sample)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--prefill-two-tiles", action="store_true",
+                    help="config3: the two-query-tile prefill kernel")
     ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
                                            "meta"],
                     default="config2")
