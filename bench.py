@@ -454,7 +454,11 @@ def ours_arm(args):
                      f"process group is torn down"}
     elif engine is not None:
         engine["tp_parity"] = None
-    prefill = prefill_measure(dev, 20, 3) if world == 1 and not args.no_prefill else None
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        N.lib().b200_set_prefill_two_tiles(1 if args.prefill_two_tiles else 0)
+        prefill = prefill_measure(dev, 20, 3)
+        prefill["two_query_tiles"] = bool(args.prefill_two_tiles)
     peak, peak_kind = load_peaks()
     ms_per_step = elapsed_ms / args.steps
     value = world * total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -515,6 +519,7 @@ def config3_arm(args):
     from llm_serving_b200 import paged_ops
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    pkg._native.lib().b200_set_prefill_two_tiles(1 if args.prefill_two_tiles else 0)
     full = pkg.workloads.config3(seed=0)
     npre = 16
     pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
@@ -583,6 +588,7 @@ def config3_arm(args):
                                       "peak": peak, "unit": "TFLOP/s",
                                       "frac": round(tflops / peak, 4)}},
         "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
+        "prefill_kernel": "two query tiles per item" if args.prefill_two_tiles else "one query tile per item",
         "device_status": paged_ops.read_status(dev),
     }
     if not args.no_cpu:
@@ -1149,6 +1155,8 @@ def main():
                     help="skip the prefill-kernel leg of the default run")
     ap.add_argument("--engine-steps", type=int, default=600,
                     help="timed engine steps of the config-5 leg of the default run")
+    ap.add_argument("--prefill-two-tiles", action="store_true",
+                    help="the two-query-tile prefill kernel (config3 and the prefill leg)")
     ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
                                            "meta"],
                     default="config2")

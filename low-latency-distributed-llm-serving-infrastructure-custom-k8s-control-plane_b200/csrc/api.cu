@@ -131,6 +131,7 @@ int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows
 // Process-wide tuning knobs (b200_set_decode_split_tokens, b200_set_prefill_cuda_cores).
 std::atomic<int> g_split_override{0};
 std::atomic<bool> g_force_cuda_core_prefill{false};
+std::atomic<bool> g_prefill_two_tiles{false};
 
 struct DecodePlan {
   bool tensor_cores;
@@ -552,11 +553,14 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     if (rc != B200_OK) return rc;
     rc = cache_tensor_map(p.value_cache, p.geom, 16, &vm);
     if (rc != B200_OK) return rc;
+    // the two-tile kernel takes query tiles in pairs (the work list, sized for single tiles,
+    // holds the pairs as well)
+    const bool two_tiles = g_prefill_two_tiles.load(std::memory_order_relaxed);
     b200::PrefillPlanArgs pa{};
     pa.cu_q = p.cu_seqlens;
     pa.skip_single = pl.split_decodes ? 1 : 0;
     pa.S = p.num_seqs;
-    pa.tq = pl.tq;
+    pa.tq = two_tiles ? 2 * pl.tq : pl.tq;
     pa.hkv = p.geom.num_kv_heads;
     pa.max_work = static_cast<int32_t>(pl.max_work);
     pa.status = p.status_word;
@@ -589,9 +593,11 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     a.hdr = hdr;
     a.work = work;
     const int64_t max_items = pl.max_work * p.geom.num_kv_heads;
-    e = b200::launch_prefill_tc(p.geom.dtype, p.geom.head_dim, qm, km, vm, a,
-                                static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30)),
-                                num_sms(), st);
+    const int items = static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30));
+    e = two_tiles ? b200::launch_prefill_q2(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items,
+                                            num_sms(), st)
+                  : b200::launch_prefill_tc(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items,
+                                            num_sms(), st);
     if (e != cudaSuccess) return cuda_fail(e, "prefill");
     return B200_OK;
   }
@@ -622,6 +628,10 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
   cudaError_t e = b200::launch_row(p.geom.dtype, a, p.num_tokens, st);
   if (e != cudaSuccess) return cuda_fail(e, "paged_prefill(row)");
   return B200_OK;
+}
+
+void b200_set_prefill_two_tiles(int32_t enable) {
+  g_prefill_two_tiles.store(enable != 0, std::memory_order_relaxed);
 }
 
 void b200_set_prefill_cuda_cores(int32_t enable) {

@@ -135,6 +135,12 @@ cudaError_t launch_prefill_tc(int dtype, int head_dim, const CUtensorMap& qm,
                               const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
                               int max_items, int num_sms, cudaStream_t stream);
 
+// Two query tiles per work item, one per softmax warpgroup (prefill_q2.cu); the plan counts
+// items in pairs of tiles.
+cudaError_t launch_prefill_q2(int dtype, int head_dim, const CUtensorMap& qm,
+                              const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
+                              int max_items, int num_sms, cudaStream_t stream);
+
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(int dtype, int head_dim, const CUtensorMap& km, const CUtensorMap& vm,
                              const DecodeArgs& a, int max_items, cudaStream_t stream);

@@ -188,9 +188,10 @@ def test_prefill_mixed_bf16(pkg, oracle, ops):
     assert np.abs(out.float().cpu().numpy() - ref).max() <= BF16_ABS
 
 
-def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False):
+def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=False):
     lib = pkg._native.lib()
     lib.b200_set_prefill_cuda_cores(1 if cuda_cores else 0)
+    lib.b200_set_prefill_two_tiles(1 if two_tiles else 0)
     try:
         q, kc, vc, bt, ctx = device_batch(b, dtype, seed)
         cu = torch.from_numpy(b.cu_seqlens()).cuda()
@@ -206,6 +207,7 @@ def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False):
         return got
     finally:
         lib.b200_set_prefill_cuda_cores(0)
+        lib.b200_set_prefill_two_tiles(0)
 
 
 @pytest.mark.parametrize("hd,bs,hq,hkv,ctx,cnt", [
@@ -217,10 +219,11 @@ def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False):
     (128, 16, 8, 8, [300, 129], [150, 129]),                                # MHA (128 tokens/tile)
     (128, 16, 32, 16, [260, 40], [260, 7]),                                 # GQA 2
 ])
-def test_prefill_tcgen05_parity(pkg, oracle, ops, hd, bs, hq, hkv, ctx, cnt):
+@pytest.mark.parametrize("two_tiles", [False, True])
+def test_prefill_tcgen05_parity(pkg, oracle, ops, hd, bs, hq, hkv, ctx, cnt, two_tiles):
     b = pkg.workloads.custom(seed=sum(cnt), context_lens=ctx, new_token_counts=cnt,
                              num_query_heads=hq, num_kv_heads=hkv, head_dim=hd, block_size=bs)
-    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd + hq)
+    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd + hq, two_tiles=two_tiles)
 
 
 def test_prefill_tcgen05_f16_and_agrees_with_cuda_cores(pkg, oracle, ops):
@@ -232,14 +235,15 @@ def test_prefill_tcgen05_f16_and_agrees_with_cuda_cores(pkg, oracle, ops):
     assert np.abs(tc - cc).max() <= BF16_ABS
 
 
-def test_prefill_config3_subset(pkg, oracle, ops):
+@pytest.mark.parametrize("two_tiles", [False, True])
+def test_prefill_config3_subset(pkg, oracle, ops, two_tiles):
     """4 of config 3's prefill chunks (on their cached prefixes) packed with 16 of its decodes."""
     full = pkg.workloads.config3(seed=0)
     idx = [0, 1, 2, 3] + list(range(16, 32))
     b = pkg.workloads.custom(seed=3, context_lens=full.context_lens[idx],
                              new_token_counts=full.new_token_counts[idx], num_query_heads=32,
                              num_kv_heads=8, head_dim=128, block_size=16)
-    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=4)
+    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=4, two_tiles=two_tiles)
 
 
 def test_masked_kernel_random_masks(oracle, ops):
