@@ -456,9 +456,9 @@ def ours_arm(args):
         engine["tp_parity"] = None
     prefill = None
     if world == 1 and not args.no_prefill:
-        N.lib().b200_set_prefill_two_tiles(1 if args.prefill_two_tiles else 0)
+        N.lib().b200_set_prefill_two_tiles(0 if args.prefill_one_tile else 1)
         prefill = prefill_measure(dev, 20, 3)
-        prefill["two_query_tiles"] = bool(args.prefill_two_tiles)
+        prefill["two_query_tiles"] = not args.prefill_one_tile
     peak, peak_kind = load_peaks()
     ms_per_step = elapsed_ms / args.steps
     value = world * total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -519,7 +519,7 @@ def config3_arm(args):
     from llm_serving_b200 import paged_ops
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    pkg._native.lib().b200_set_prefill_two_tiles(1 if args.prefill_two_tiles else 0)
+    pkg._native.lib().b200_set_prefill_two_tiles(0 if args.prefill_one_tile else 1)
     full = pkg.workloads.config3(seed=0)
     npre = 16
     pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
@@ -588,7 +588,7 @@ def config3_arm(args):
                                       "peak": peak, "unit": "TFLOP/s",
                                       "frac": round(tflops / peak, 4)}},
         "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
-        "prefill_kernel": "two query tiles per item" if args.prefill_two_tiles else "one query tile per item",
+        "prefill_kernel": "one query tile per item" if args.prefill_one_tile else "two query tiles per item",
         "device_status": paged_ops.read_status(dev),
     }
     if not args.no_cpu:
@@ -1155,8 +1155,9 @@ def main():
                     help="skip the prefill-kernel leg of the default run")
     ap.add_argument("--engine-steps", type=int, default=600,
                     help="timed engine steps of the config-5 leg of the default run")
-    ap.add_argument("--prefill-two-tiles", action="store_true",
-                    help="the two-query-tile prefill kernel (config3 and the prefill leg)")
+    ap.add_argument("--prefill-one-tile", action="store_true",
+                    help="the one-query-tile prefill kernel instead of the default two-tile one "
+                         "(config3 and the prefill leg)")
     ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
                                            "meta"],
                     default="config2")

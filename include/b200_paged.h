@@ -192,8 +192,9 @@ int b200_paged_prefill(const B200PrefillParams* p, void* workspace, size_t works
  * (for A/B comparison); 0 restores the default. */
 void b200_set_prefill_cuda_cores(int32_t enable);
 
-/* Nonzero: run the tensor-core prefill with two query tiles per work item, one per softmax
- * warpgroup (each K/V tile staged once for both); 0 restores the default one-tile kernel. */
+/* Which tensor-core prefill kernel runs: nonzero (the default) = two query tiles per work item,
+ * one per softmax warpgroup, each K/V tile staged once for both; 0 = one query tile per work item
+ * with the K/V tiles alternating between the softmax warpgroups (kept for A/B comparison). */
 void b200_set_prefill_two_tiles(int32_t enable);
 
 /* ============================================================================================

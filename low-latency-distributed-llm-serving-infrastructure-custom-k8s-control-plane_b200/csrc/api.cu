@@ -131,7 +131,7 @@ int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows
 // Process-wide tuning knobs (b200_set_decode_split_tokens, b200_set_prefill_cuda_cores).
 std::atomic<int> g_split_override{0};
 std::atomic<bool> g_force_cuda_core_prefill{false};
-std::atomic<bool> g_prefill_two_tiles{false};
+std::atomic<bool> g_prefill_two_tiles{true};
 
 struct DecodePlan {
   bool tensor_cores;

@@ -1,6 +1,6 @@
-// K3 variant, selected by b200_set_prefill_two_tiles (off by default; compiled for sm_100a with no
-// spills, not yet run on a GPU): two 128-row query tiles per work item, one per softmax warpgroup,
-// against one stream of 128-key K/V tiles.
+// K3, the default tensor-core prefill (b200_set_prefill_two_tiles(0) selects the one-tile kernel
+// of prefill.cu instead): two 128-row query tiles per work item, one per softmax warpgroup, against
+// one stream of 128-key K/V tiles.
 //
 // One work item = (sequence, pair of query tiles of TQ = 128/G tokens each, KV head).  Softmax
 // warpgroup w owns query tile w (rows g*TQ + t of tokens [t_begin + w*TQ, t_begin + (w+1)*TQ)) for

@@ -188,7 +188,7 @@ def test_prefill_mixed_bf16(pkg, oracle, ops):
     assert np.abs(out.float().cpu().numpy() - ref).max() <= BF16_ABS
 
 
-def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=False):
+def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=True):
     lib = pkg._native.lib()
     lib.b200_set_prefill_cuda_cores(1 if cuda_cores else 0)
     lib.b200_set_prefill_two_tiles(1 if two_tiles else 0)
@@ -207,7 +207,7 @@ def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=
         return got
     finally:
         lib.b200_set_prefill_cuda_cores(0)
-        lib.b200_set_prefill_two_tiles(0)
+        lib.b200_set_prefill_two_tiles(1)  # the default
 
 
 @pytest.mark.parametrize("hd,bs,hq,hkv,ctx,cnt", [
