@@ -45,6 +45,49 @@ static float dot_row(const float* a, const float* b, int32_t n) {
     return acc;
 }
 
+/* The same arithmetic as dot_row for 8 keys at once: kt holds the keys transposed ([d][8]), so
+ * lane j accumulates q[d] * k_j[d] over d in the same sequential order dot_row uses, and the
+ * compiler may put the 8 independent sums in one SIMD register (no reassociation). */
+static void dot_rows8(const float* q, const float* kt, int32_t n, float* out8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int32_t d = 0; d < n; ++d) {
+        const float qd = q[d];
+#pragma omp simd
+        for (int32_t j = 0; j < 8; ++j) acc[j] += qd * kt[d * 8 + j];
+    }
+    for (int32_t j = 0; j < 8; ++j) out8[j] = acc[j];
+}
+
+/* softmax_pv_row with the PV product taken key by key: out[d] still receives
+ * scores[0]*v_0[d] + scores[1]*v_1[d] + ... in that order, one rounding per step, so the result
+ * is bit-identical; the loop over d is what vectorises.  `acc` holds head_dim floats. */
+static void softmax_pv_row_by_key(float* scores, int32_t n, float max_score,
+                                  const float* const* v_rows, int32_t head_dim, float* acc,
+                                  float* out_row) {
+    if (max_score == -INFINITY) max_score = 0.0f;
+    float total = 0.0f;
+    for (int32_t c = 0; c < n; ++c) {
+        if (scores[c] > -1e30f) {
+            scores[c] = expf(scores[c] - max_score);
+            total += scores[c];
+        } else {
+            scores[c] = 0.0f;
+        }
+    }
+    if (total > 0.0f) {
+        const float inv = 1.0f / total;
+        for (int32_t c = 0; c < n; ++c) scores[c] *= inv;
+    }
+    for (int32_t d = 0; d < head_dim; ++d) acc[d] = 0.0f;
+    for (int32_t c = 0; c < n; ++c) {
+        const float pc = scores[c];
+        const float* v = v_rows[c];
+#pragma omp simd
+        for (int32_t d = 0; d < head_dim; ++d) acc[d] += pc * v[d];
+    }
+    for (int32_t d = 0; d < head_dim; ++d) out_row[d] = acc[d];
+}
+
 void oracle_paged_attention(const float* query, const float* key_cache, const float* value_cache,
                             int32_t layer_idx, OraclePagedDims dims, const int32_t* gather_slots,
                             const uint8_t* attention_mask, float scaling, float* output,
@@ -99,39 +142,78 @@ void oracle_paged_ragged(const float* q, const float* key_cache, const float* va
     first_token[0] = 0;                       /* cu_seqlens, app/model/paged_attention.py:121-125 */
     for (int32_t s = 0; s < num_seqs; ++s) first_token[s + 1] = first_token[s] + new_token_counts[s];
 
-#pragma omp parallel for schedule(dynamic, 1)
-    for (int32_t s = 0; s < num_seqs; ++s) {
-        const int32_t start = start_positions[s], count = new_token_counts[s];
-        const int32_t ctx = start + count;
-        const int32_t* bt = block_tables + (int64_t)s * block_table_stride;
-        const size_t cap = (size_t)(ctx > 0 ? ctx : 1);
-        float* sc = (float*)malloc(sizeof(float) * cap);
-        int64_t* slots = (int64_t*)malloc(sizeof(int64_t) * cap);
-        const float** vr = (const float**)malloc(sizeof(float*) * cap);
-        for (int32_t p = 0; p < ctx; ++p)     /* slot = block*BS + offset, manager.py:320-333 */
-            slots[p] = (int64_t)bt[p / block_size] * block_size + p % block_size;
-        for (int32_t i = 0; i < count; ++i) {
-            const int64_t tok = first_token[s] + i;
-            const int32_t pos = start + i;    /* causal window, paged_attention.py:108-115 */
-            for (int32_t h = 0; h < num_query_heads; ++h) {
-                const int64_t koff = (int64_t)(h / group) * head_dim;
-                const float* qrow = q + (tok * num_query_heads + h) * head_dim;
-                float mx = -INFINITY;
-                for (int32_t p = 0; p <= pos; ++p) {
-                    const float sv = dot_row(qrow, lk + slots[p] * row + koff, head_dim) * scaling;
-                    sc[p] = sv;
-                    if (sv > mx) mx = sv;
-                    vr[p] = lv + slots[p] * row + koff;
+    int32_t max_ctx = 1;
+    for (int32_t s = 0; s < num_seqs; ++s)
+        if (start_positions[s] + new_token_counts[s] > max_ctx)
+            max_ctx = start_positions[s] + new_token_counts[s];
+    const int64_t num_tokens = first_token[num_seqs];
+
+    /* One task per new token (not per sequence), so a batch of a few long chunks still spreads
+     * over every core; each row's arithmetic and its order are unchanged. */
+#pragma omp parallel
+    {
+        float* sc = (float*)malloc(sizeof(float) * (size_t)max_ctx * (size_t)group);
+        const float** vr = (const float**)malloc(sizeof(float*) * (size_t)max_ctx);
+        float* kt = (float*)malloc(sizeof(float) * 8 * (size_t)head_dim);
+        float* acc = (float*)malloc(sizeof(float) * (size_t)head_dim);
+#pragma omp for schedule(dynamic, 4)
+        for (int64_t tok = 0; tok < num_tokens; ++tok) {
+            int32_t lo = 0, hi = num_seqs; /* sequence of this token: first_token[s] <= tok */
+            while (hi - lo > 1) {
+                const int32_t mid = (lo + hi) / 2;
+                if (first_token[mid] <= tok) lo = mid; else hi = mid;
+            }
+            const int32_t s = lo;
+            const int32_t* bt = block_tables + (int64_t)s * block_table_stride;
+            /* causal window [0, pos], paged_attention.py:108-115 */
+            const int32_t pos = start_positions[s] + (int32_t)(tok - first_token[s]);
+            const int32_t n = pos + 1;
+            for (int32_t g = 0; g < num_kv_heads; ++g) {
+                const int64_t koff = (int64_t)g * head_dim;
+                /* scores of the group's query heads: sc[hh * max_ctx + p] */
+                int32_t p = 0;
+                for (; p + 8 <= n; p += 8) {
+                    for (int32_t j = 0; j < 8; ++j) {
+                        /* slot = block*BS + offset, manager.py:320-333 */
+                        const int32_t pj = p + j;
+                        const int64_t slot = (int64_t)bt[pj / block_size] * block_size + pj % block_size;
+                        const float* kr = lk + slot * row + koff;
+                        for (int32_t d = 0; d < head_dim; ++d) kt[d * 8 + j] = kr[d];
+                    }
+                    for (int32_t hh = 0; hh < group; ++hh) {
+                        const float* qrow = q + (tok * num_query_heads + g * group + hh) * head_dim;
+                        float d8[8];
+                        dot_rows8(qrow, kt, head_dim, d8);
+                        for (int32_t j = 0; j < 8; ++j) sc[(int64_t)hh * max_ctx + p + j] = d8[j] * scaling;
+                    }
                 }
-                /* Masked columns (p > pos) contribute exact zeros in the reference's PV loop, so
-                 * the window [0, pos] gives bit-identical rows. */
-                softmax_pv_row(sc, pos + 1, mx, vr, head_dim,
-                               out + (tok * num_query_heads + h) * head_dim);
+                for (; p < n; ++p) {
+                    const int64_t slot = (int64_t)bt[p / block_size] * block_size + p % block_size;
+                    for (int32_t hh = 0; hh < group; ++hh) {
+                        const float* qrow = q + (tok * num_query_heads + g * group + hh) * head_dim;
+                        sc[(int64_t)hh * max_ctx + p] = dot_row(qrow, lk + slot * row + koff, head_dim) * scaling;
+                    }
+                }
+                for (int32_t c = 0; c < n; ++c) {
+                    const int64_t slot = (int64_t)bt[c / block_size] * block_size + c % block_size;
+                    vr[c] = lv + slot * row + koff;
+                }
+                for (int32_t hh = 0; hh < group; ++hh) {
+                    float* srow = sc + (int64_t)hh * max_ctx;
+                    float mx = -INFINITY;
+                    for (int32_t c = 0; c < n; ++c)
+                        if (srow[c] > mx) mx = srow[c];
+                    /* Masked columns (c > pos) contribute exact zeros in the reference's PV loop,
+                     * so the window [0, pos] gives bit-identical rows. */
+                    softmax_pv_row_by_key(srow, n, mx, vr, head_dim, acc,
+                                          out + (tok * num_query_heads + g * group + hh) * head_dim);
+                }
             }
         }
         free(sc);
-        free(slots);
         free(vr);
+        free(kt);
+        free(acc);
     }
     free(first_token);
 }
