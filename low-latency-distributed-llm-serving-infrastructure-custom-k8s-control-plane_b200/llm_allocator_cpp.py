@@ -37,11 +37,13 @@ class PageAllocator:
                                                 int(bytes_per_token), int(total_cpu_blocks),
                                                 ctypes.byref(h)))
         self._h = h
+        # bound now: at interpreter exit this module's globals may be gone before __del__ runs
+        self._destroy = N.lib().b200_host_allocator_destroy
 
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            N.lib().b200_host_allocator_destroy(h)
+            self._destroy(h)
             self._h = None
 
     def allocate_block(self) -> int:
