@@ -635,8 +635,13 @@ def engine4_arm(args):
     from llm_serving_b200.engine import build_engine
     from llm_serving_b200.model import CONFIG4, kv_bytes_per_token
     world, rank, dev = _dist_setup()
-    arrivals, prompts, olens = pkg.workloads.config4_requests(args.requests, args.rate,
+    # rate <= 0: every request arrives at t=0 (closed loop: the engine's capacity, not the
+    # offered load); the prompts and output lengths do not depend on the rate
+    arrivals, prompts, olens = pkg.workloads.config4_requests(args.requests,
+                                                              args.rate if args.rate > 0 else 20.0,
                                                               CONFIG4.vocab)
+    if args.rate <= 0:
+        arrivals = np.zeros_like(arrivals)
     nreq = args.requests
     blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(CONFIG4, world) * 16))
     eng = build_engine(CONFIG4, total_blocks=blocks, block_size=16, rank=rank, world=world,
@@ -690,14 +695,103 @@ def engine4_arm(args):
         "metric": "engine output tokens/s (config 4)", "value": round(out_tokens / elapsed, 1),
         "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
         "scaling": "strong" if world > 1 else "n/a", "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"config4 engine, first {nreq} of 2000 Poisson({args.rate}/s) "
-                               "requests, prompts lognormal(512) <= 4096, outputs U[64,512], "
+        "config": {"workload": f"config4 engine, first {nreq} of 2000 requests, "
+                               + (f"Poisson({args.rate}/s) arrivals" if args.rate > 0 else
+                                  "all submitted at t=0 (closed loop)")
+                               + ", prompts lognormal(512) <= 4096, outputs U[64,512], "
                                "max 256 decoding sequences, random-init 16x2048 Llama",
                    "parallelism": f"tp{world}", "kv_pool_blocks": blocks},
         "elapsed_s": round(elapsed, 3), "output_tokens": out_tokens, "steps": eng.steps,
         "graph_steps": graph_steps, "preemptions": eng.scheduler.preemption_count,
         "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 2) if ttft else None,
         "tpot_ms_p50": round(1e3 * float(np.median(tpot)), 3) if tpot else None,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def reference_engine4_arm(args):
+    """`--workload engine4 --impl reference`: the reference's own engine on one B200, the engine
+    baseline for config 4.  Its LLMEngine + Scheduler + PagedKVCacheManager (app/, staged
+    unmodified into oracle/_ref by `make -C oracle ref`) with its own compiled allocator binding
+    (oracle/_ref/llm_allocator_cpp*.so) and its own CudaKVCacheStrategy
+    (app/memory/strategies.py:100-129); the engine is built directly, because the reference's
+    configure_runtime rejects CUDA (app/config.py:35-36).  The model is a transformers Llama of
+    the config-4 architecture, random init, bf16, attention through the reference's paged hook on
+    its SDPA path (app/model/paged_attention.py:138-180).  The first `--requests` requests of the
+    seeded config-4 stream are submitted at t=0, and steps run until they finish or `--seconds`
+    pass.  Compare with `--workload engine4 --rate 0 --requests N` (this package's engine on the
+    same requests).  Rank 0 only."""
+    import glob
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    ref_parent = os.path.join(ROOT, "oracle", "_ref")
+    binding = glob.glob(os.path.join(ref_parent, "llm_allocator_cpp*.so"))
+    if not (os.path.isfile(os.path.join(ref_parent, "app", "engine", "llm_engine.py")) and binding):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference engine is not staged "
+                          "(make -C oracle ref, which needs a reference checkout)"}))
+        return 0
+    import torch
+    sys.path.insert(0, ref_parent)
+    import llm_allocator_cpp  # noqa: F401  (the compiled reference binding)
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from app.engine.llm_engine import LLMEngine
+    from app.memory.manager import PagedKVCacheManager
+    from app.scheduler.scheduler import Scheduler
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_serving_b200.model import CONFIG4 as shape, kv_bytes_per_token
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    _, prompts, olens = pkg.workloads.config4_requests(args.requests, 20.0, shape.vocab)
+    cfg = LlamaConfig(vocab_size=shape.vocab, hidden_size=shape.hidden,
+                      intermediate_size=shape.ffn, num_hidden_layers=shape.num_layers,
+                      num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
+                      head_dim=shape.head_dim, max_position_embeddings=8192,
+                      rms_norm_eps=shape.rms_eps, rope_theta=shape.rope_theta)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(shape) * 16))
+    kv = PagedKVCacheManager.from_model_config(cfg, total_blocks=blocks, block_size=16,
+                                               dtype=torch.bfloat16, device=str(dev))
+    sched = Scheduler(kv_cache_manager=kv, max_batch_size=256, max_num_batched_tokens=16384,
+                      block_size=16, max_model_len=8192)
+    eng = LLMEngine(kv_cache_manager=kv, scheduler=sched, model=model)
+    for i in range(2):  # warm-up outside the timed run
+        eng.add_request(prompt_token_ids=prompts[i][:64], max_tokens=4)
+    while eng.has_unfinished_requests():
+        eng.step()
+    torch.cuda.synchronize(dev)
+    seqs = [eng.add_request(prompt_token_ids=p, max_tokens=int(o))
+            for p, o in zip(prompts, olens[:args.requests])]
+    steps = 0
+    t0 = time.perf_counter()
+    while eng.has_unfinished_requests() and time.perf_counter() - t0 < args.seconds:
+        eng.step()
+        steps += 1
+    torch.cuda.synchronize(dev)
+    elapsed = time.perf_counter() - t0
+    out_tokens = sum(len(s.output_token_ids) for s in seqs)
+    value = out_tokens / elapsed
+    line = {
+        "impl": "reference", "metric": "engine output tokens/s (config 4)",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config4 engine, first {args.requests} of 2000 requests all "
+                               "submitted at t=0 (closed loop), prompts lognormal(512) <= 4096, "
+                               "outputs U[64,512], max 256 decoding sequences, random-init "
+                               "16x2048 Llama", "kv_pool_blocks": blocks,
+                   "engine": "reference LLMEngine + Scheduler + PagedKVCacheManager "
+                             "(CudaKVCacheStrategy, compiled reference allocator), transformers "
+                             "Llama through the reference's paged hook (SDPA path), on the GPU"},
+        "output_tokens": out_tokens, "finished": sum(1 for s in seqs if s.is_finished()),
+        "requests": args.requests, "steps": steps, "elapsed_s": round(elapsed, 2),
+        "time_box_s": args.seconds, "preemptions": sched.preemption_count,
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
     return 0
@@ -1162,13 +1256,16 @@ def main():
                                            "meta"],
                     default="config2")
     ap.add_argument("--requests", type=int, default=200, help="engine4: requests to run")
-    ap.add_argument("--rate", type=float, default=20.0, help="engine4: arrivals per second")
+    ap.add_argument("--rate", type=float, default=20.0,
+                    help="engine4: arrivals per second (<= 0: all requests at t=0)")
+    ap.add_argument("--seconds", type=float, default=120.0,
+                    help="engine4 --impl reference: time box of the reference engine's run")
     ap.add_argument("--kv-gb", type=float, default=40.0, help="engine: KV pool GB per GPU")
     args = ap.parse_args()
     if args.workload == "config3":
         return config3_arm(args)
     if args.workload == "engine4":
-        return engine4_arm(args)
+        return reference_engine4_arm(args) if args.impl == "reference" else engine4_arm(args)
     if args.workload == "engine5":
         return engine5_arm(args)
     if args.workload == "swap":
