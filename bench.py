@@ -733,6 +733,11 @@ def reference_engine4_arm(args):
                           "(make -C oracle ref, which needs a reference checkout)"}))
         return 0
     import torch
+    # The reference pins torch 2.13; its CudaKVCacheStrategy enters torch.cuda._device_ctx(index)
+    # (app/memory/strategies.py:112,118), which this image's torch lacks: torch.cuda.device(index)
+    # is the same context manager.
+    if not hasattr(torch.cuda, "_device_ctx"):
+        torch.cuda._device_ctx = torch.cuda.device
     sys.path.insert(0, ref_parent)
     import llm_allocator_cpp  # noqa: F401  (the compiled reference binding)
     from transformers import LlamaConfig, LlamaForCausalLM

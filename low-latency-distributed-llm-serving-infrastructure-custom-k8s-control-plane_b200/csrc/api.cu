@@ -558,6 +558,7 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     const bool two_tiles = g_prefill_two_tiles.load(std::memory_order_relaxed);
     b200::PrefillPlanArgs pa{};
     pa.cu_q = p.cu_seqlens;
+    pa.ctx_lens = p.context_lens;
     pa.skip_single = pl.split_decodes ? 1 : 0;
     pa.S = p.num_seqs;
     pa.tq = two_tiles ? 2 * pl.tq : pl.tq;

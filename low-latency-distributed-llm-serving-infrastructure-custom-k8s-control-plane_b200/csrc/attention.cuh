@@ -104,6 +104,9 @@ struct PrefillHeader {
 
 struct PrefillPlanArgs {
   const int64_t* cu_q;
+  // context lengths: when given, the work list is ordered by decreasing cost (KV tiles per
+  // item), so that the kernels' snake traversal hands every CTA a near-equal share
+  const int32_t* ctx_lens;
   int32_t skip_single;  // sequences with one new token go to the decode kernel instead
   int32_t S;
   int32_t tq;
@@ -131,6 +134,15 @@ struct PrefillArgs {
 };
 
 cudaError_t launch_prefill_plan(const PrefillPlanArgs& a, cudaStream_t stream);
+
+// Work item of CTA blockIdx.x in traversal round `round` of a persistent prefill kernel: rounds
+// alternate direction over the CTAs (snake order), so with the work list sorted by decreasing
+// cost the CTA that got the largest item of one round gets the smallest of the next.
+__device__ __forceinline__ int snake_item(int round) {
+  const int g = static_cast<int>(gridDim.x);
+  return round * g + ((round & 1) ? (g - 1 - static_cast<int>(blockIdx.x))
+                                  : static_cast<int>(blockIdx.x));
+}
 cudaError_t launch_prefill_tc(int dtype, int head_dim, const CUtensorMap& qm,
                               const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
                               int max_items, int num_sms, cudaStream_t stream);

@@ -106,21 +106,36 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, vol
 
 }  // namespace
 
+// Cost bins of the work-list sort: an item's cost is the number of 128-key KV tiles it reads,
+// clamped to the last bin (items that long are ordered among themselves arbitrarily).
+constexpr int kCostBins = 512;
+
+__device__ __forceinline__ int pair_cost(const PrefillPlanArgs& a, int s, int64_t count, int k) {
+  const int64_t tb = static_cast<int64_t>(k) * a.tq;
+  const int64_t n = count - tb < a.tq ? count - tb : a.tq;
+  const int64_t kv_end = a.ctx_lens[s] - count + tb + n;
+  const int64_t c = (kv_end + kBN - 1) / kBN;
+  return c < 0 ? 0 : (c >= kCostBins ? kCostBins - 1 : static_cast<int>(c));
+}
+
 __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
   __shared__ int32_t warp_sums[32];
   __shared__ int32_t carry_s;
+  __shared__ int32_t bins[kCostBins];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool sorted = a.ctx_lens != nullptr;
   if (tid == 0) carry_s = 0;
+  for (int b = tid; b < kCostBins; b += 1024) bins[b] = 0;
   __syncthreads();
+  auto items_of = [&](int s) -> int32_t {
+    const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
+    return (count > 0 && !(a.skip_single && count == 1))
+               ? static_cast<int32_t>((count + a.tq - 1) / a.tq)
+               : 0;
+  };
   for (int base = 0; base < a.S; base += 1024) {
     const int s = base + tid;
-    int32_t n = 0;
-    if (s < a.S) {
-      const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
-      n = (count > 0 && !(a.skip_single && count == 1))
-              ? static_cast<int32_t>((count + a.tq - 1) / a.tq)
-              : 0;
-    }
+    const int32_t n = s < a.S ? items_of(s) : 0;
     int32_t v = n;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -141,13 +156,55 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
     __syncthreads();
     const int32_t incl = v + (warp > 0 ? warp_sums[warp - 1] : 0) + carry_s;
     const int32_t excl = incl - n;
-    if (s < a.S)
-      for (int32_t k = 0; k < n; ++k)
-        if (excl + k < a.max_work) a.work[excl + k] = make_int2(s, k);
-        else flag_status(a.status, B200_DEVICE_BAD_OP);
+    if (s < a.S) {
+      if (sorted) {
+        const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
+        for (int32_t k = 0; k < n; ++k) atomicAdd(&bins[pair_cost(a, s, count, k)], 1);
+      } else {
+        for (int32_t k = 0; k < n; ++k)
+          if (excl + k < a.max_work) a.work[excl + k] = make_int2(s, k);
+          else flag_status(a.status, B200_DEVICE_BAD_OP);
+      }
+    }
     __syncthreads();
     if (tid == 1023) carry_s = incl;
     __syncthreads();
+  }
+  if (sorted) {
+    // start offset of every bin in decreasing-cost order (warp 0: 16 bins per lane, then a scan
+    // across the lanes), then each item is placed at its bin's next free position
+    if (warp == 0) {
+      constexpr int kPer = kCostBins / 32;
+      int32_t local[kPer];
+      int32_t sum = 0;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        local[i] = bins[kCostBins - 1 - (lane * kPer + i)];
+        sum += local[i];
+      }
+      int32_t v = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      int32_t off = v - sum;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        bins[kCostBins - 1 - (lane * kPer + i)] = off;
+        off += local[i];
+      }
+    }
+    __syncthreads();
+    for (int s = tid; s < a.S; s += 1024) {
+      const int32_t n = items_of(s);
+      const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
+      for (int32_t k = 0; k < n; ++k) {
+        const int32_t pos = atomicAdd(&bins[pair_cost(a, s, count, k)], 1);
+        if (pos < a.max_work) a.work[pos] = make_int2(s, k);
+        else flag_status(a.status, B200_DEVICE_BAD_OP);
+      }
+    }
   }
   if (tid == 0) {
     const int32_t tiles = carry_s < a.max_work ? carry_s : a.max_work;
@@ -250,7 +307,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
       const int32_t layer_base = a.layer * a.nb;
       uint32_t n_items = 0, kv_it = 0, q_issued = 0;
-      for (int item = blockIdx.x; item < total; item += gridDim.x) {
+      for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
         int s, h, q_row0, n_q, pos0, kv_end, ctx;
         decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
         if (is_k) {
@@ -381,7 +438,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
         return true;
       };
-      for (int item = blockIdx.x; item < total; item += gridDim.x) {
+      for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
         int s, h, q_row0, n_q, pos0, kv_end, ctx;
         decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
         const int n_kv = (kv_end + kBN - 1) / kBN;
@@ -443,7 +500,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const int sm_tid = (warp & 3) * 32 + lane;  // 0..127 within the warpgroup
     float2* xch = reinterpret_cast<float2*>(smem + L.xch);
     uint32_t s_it = 0, kv_it = 0, n_items = 0;
-    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+    for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
       int s, h, q_row0, n_q, pos0, kv_end, ctx;
       decode_item(item, s, h, q_row0, n_q, pos0, kv_end, ctx);
       const int n_kv = (kv_end + kBN - 1) / kBN;

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
       const int32_t layer_base = a.layer * a.nb;
       uint32_t n_items = 0, kv_it = 0, q_issued = 0;
-      for (int item = blockIdx.x; item < total; item += gridDim.x) {
+      for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
         const Q2Item it = q2_decode(a, item);
         if (is_k) {
           if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                              a.status);
       };
       bool ok = true;
-      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      for (int round = 0, item = snake_item(0); item < total && ok; item = snake_item(++round)) {
         const Q2Item it = q2_decode(a, item);
         const int n_kv = it.n_kv_all;
         const int zw = q2_zero_wg(it);
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const uint32_t o_self = trow + kColO + wg * D;
     const int sm_tid = quarter * 32 + lane;
     uint32_t c_tile = 0, kv_it = 0, n_items = 0;
-    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+    for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
       const Q2Item it = q2_decode(a, item);
       const int n_kv = wg ? it.n_kv[1] : it.n_kv[0];
       const int n_q = wg ? it.n_q[1] : it.n_q[0];

@@ -13,6 +13,16 @@ def staged() -> bool:
     return os.path.isfile(os.path.join(REF_APP_PARENT, "app", "engine", "llm_engine.py"))
 
 
+def torch_compat():
+    """The reference pins torch 2.13 (requirements.txt:65); its CudaKVCacheStrategy enters
+    torch.cuda._device_ctx(index) (app/memory/strategies.py:112,118), a private helper this
+    image's torch 2.11 does not have.  torch.cuda.device(index) is the same context manager (the
+    device is current inside the block), so it stands in for it; nothing else is changed."""
+    import torch
+    if not hasattr(torch.cuda, "_device_ctx"):
+        torch.cuda._device_ctx = torch.cuda.device
+
+
 def import_reference_app(binding):
     """Make `import llm_allocator_cpp` resolve to `binding`, put the staged tree first on the
     path and import the engine's modules.  One binding per process: the reference modules keep
@@ -21,6 +31,7 @@ def import_reference_app(binding):
     if current is not None and current is not binding:
         raise RuntimeError("the reference app was already imported with another binding")
     sys.modules["llm_allocator_cpp"] = binding
+    torch_compat()
     if REF_APP_PARENT not in sys.path:
         sys.path.insert(0, REF_APP_PARENT)
     import app.engine.llm_engine as llm_engine
