@@ -520,6 +520,7 @@ def config3_arm(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     pkg._native.lib().b200_set_prefill_two_tiles(0 if args.prefill_one_tile else 1)
+    pkg._native.lib().b200_set_prefill_poly_exp(args.prefill_poly_exp)
     full = pkg.workloads.config3(seed=0)
     npre = 16
     pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
@@ -589,6 +590,7 @@ def config3_arm(args):
                                       "frac": round(tflops / peak, 4)}},
         "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
         "prefill_kernel": "one query tile per item" if args.prefill_one_tile else "two query tiles per item",
+        "prefill_poly_exp_mode": args.prefill_poly_exp,
         "device_status": paged_ops.read_status(dev),
     }
     if not args.no_cpu:
@@ -924,6 +926,32 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
     }
     if clocks is not None:
         res["clocks"] = clocks
+    if world > 1:
+        # the step's exchange on its own: 2 all-reduces per layer (after o_proj and down_proj) of
+        # the decode batch's hidden states, bf16, timed back to back (max over ranks)
+        rows = max(1, min(len(eng.scheduler.running), eng.scheduler.max_batch_size))
+        x = torch.randn((rows, shape.hidden), device=dev).to(torch.bfloat16)
+        n_ar = 2 * shape.num_layers
+        for _ in range(3):
+            dist.all_reduce(x)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(10 * n_ar):
+            dist.all_reduce(x)
+        a1.record()
+        torch.cuda.synchronize(dev)
+        ar = torch.tensor([a0.elapsed_time(a1) / 10], dtype=torch.float64, device=dev)
+        dist.all_reduce(ar, op=dist.ReduceOp.MAX)
+        ar_ms = float(ar.item())
+        res["allreduce"] = {"ms_per_step": round(ar_ms, 3), "calls_per_step": n_ar,
+                            "bytes_per_call": rows * shape.hidden * 2,
+                            "share_of_mean_step": round(ar_ms / res["ms_per_step"], 4),
+                            "how": "NCCL all-reduce of the decode batch's hidden states "
+                                   "(rows x hidden, bf16), 2 per layer, timed alone back to back "
+                                   "with CUDA events, max over ranks"}
+        del x
     eng.release_graphs()  # captured graphs hold NCCL calls: release before the process group
     del eng, kv, pool
     torch.cuda.empty_cache()
@@ -1254,6 +1282,9 @@ def main():
                     help="skip the prefill-kernel leg of the default run")
     ap.add_argument("--engine-steps", type=int, default=600,
                     help="timed engine steps of the config-5 leg of the default run")
+    ap.add_argument("--prefill-poly-exp", type=int, default=1, choices=[0, 1, 2],
+                    help="config3: share of softmax exponentials on the FMA pipe (0 none, 1 a "
+                         "quarter, 2 half)")
     ap.add_argument("--prefill-one-tile", action="store_true",
                     help="the one-query-tile prefill kernel instead of the default two-tile one "
                          "(config3 and the prefill leg)")

@@ -197,6 +197,11 @@ void b200_set_prefill_cuda_cores(int32_t enable);
  * with the K/V tiles alternating between the softmax warpgroups (kept for A/B comparison). */
 void b200_set_prefill_two_tiles(int32_t enable);
 
+/* Share of the two-tile prefill's softmax exponentials computed by a cubic on the FMA pipe
+ * instead of the SFU's ex2 (relative error below 7.5e-5 either way, far under bf16's): 0 = none,
+ * 1 = one pair of keys in four (the default), 2 = one pair in two.  A tuning knob. */
+void b200_set_prefill_poly_exp(int32_t mode);
+
 /* ============================================================================================
  * 3. KV-cache slot write (reshape_and_cache)
  * ==========================================================================================*/

@@ -132,6 +132,7 @@ int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows
 std::atomic<int> g_split_override{0};
 std::atomic<bool> g_force_cuda_core_prefill{false};
 std::atomic<bool> g_prefill_two_tiles{true};
+std::atomic<int> g_prefill_poly_exp{1};
 
 struct DecodePlan {
   bool tensor_cores;
@@ -596,7 +597,8 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     const int64_t max_items = pl.max_work * p.geom.num_kv_heads;
     const int items = static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30));
     e = two_tiles ? b200::launch_prefill_q2(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items,
-                                            num_sms(), st)
+                                            num_sms(),
+                                            g_prefill_poly_exp.load(std::memory_order_relaxed), st)
                   : b200::launch_prefill_tc(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items,
                                             num_sms(), st);
     if (e != cudaSuccess) return cuda_fail(e, "prefill");
@@ -629,6 +631,10 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
   cudaError_t e = b200::launch_row(p.geom.dtype, a, p.num_tokens, st);
   if (e != cudaSuccess) return cuda_fail(e, "paged_prefill(row)");
   return B200_OK;
+}
+
+void b200_set_prefill_poly_exp(int32_t mode) {
+  g_prefill_poly_exp.store(mode < 0 || mode > 2 ? 1 : mode, std::memory_order_relaxed);
 }
 
 void b200_set_prefill_two_tiles(int32_t enable) {

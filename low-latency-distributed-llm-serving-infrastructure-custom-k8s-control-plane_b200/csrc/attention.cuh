@@ -149,9 +149,11 @@ cudaError_t launch_prefill_tc(int dtype, int head_dim, const CUtensorMap& qm,
 
 // Two query tiles per work item, one per softmax warpgroup (prefill_q2.cu); the plan counts
 // items in pairs of tiles.
+// poly_mode: share of the softmax exponentials computed on the FMA pipe instead of the SFU
+// (0 = none, 1 = one pair in four, 2 = one pair in two).
 cudaError_t launch_prefill_q2(int dtype, int head_dim, const CUtensorMap& qm,
                               const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
-                              int max_items, int num_sms, cudaStream_t stream);
+                              int max_items, int num_sms, int poly_mode, cudaStream_t stream);
 
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(int dtype, int head_dim, const CUtensorMap& km, const CUtensorMap& vm,

@@ -88,6 +88,55 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, vol
   return false;
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of math) -----
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for both lanes of a packed pair on the FMA and integer pipes, leaving the SFU (whose ex2
+// throughput, shared by both softmax warpgroups, is what the softmax otherwise waits on) to the
+// other pairs.  x = j + f with j = round(x) -- adding 1.5 * 2^23 rounds to an integer held in the
+// low mantissa bits -- and f in [-0.5, 0.5]; 2^f comes from a cubic fitted here to 2^f on that
+// interval by relative least squares (maximum relative error 7.5e-5, against bf16's 2^-9), and j
+// is added to its exponent field.  Lanes are clamped to x >= -126 first, so masked (-inf) and
+// vanishing terms give a result of at most 2^-126 instead of a wrapped exponent.
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = f2_add(x2, f2_pack(12582912.f, 12582912.f));
+  const uint64_t r = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), x2);
+  uint64_t p = f2_fma(f2_pack(0.0551716648f, 0.0551716648f), f, f2_pack(0.2426111251f, 0.2426111251f));
+  p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
+  p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
+  float t0, t1, q0, q1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(p, q0, q1);
+  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
 // One work item: sequence s, KV head h, query tiles w = 0, 1 of TQ tokens starting at q_row0.
 struct Q2Item {
   int s, h, q_row0, pos0;  // pos0: position of tile 0's first token
@@ -126,7 +175,9 @@ __device__ __forceinline__ int q2_zero_wg(const Q2Item& it) { return it.n_kv[1] 
 
 }  // namespace
 
-template <typename T, int D>
+// kPolyMask: bit i set = pair i of every 8 consecutive exponential pairs of a row is computed by
+// exp2_poly2 on the FMA pipe instead of ex2 on the SFU.
+template <typename T, int D, uint32_t kPolyMask>
 __global__ void __launch_bounds__(kPrefillThreads, 1)
     prefill_q2_kernel(const __grid_constant__ CUtensorMap qmap,
                       const __grid_constant__ CUtensorMap kmap,
@@ -447,7 +498,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
         auto max_chunk = [&](const float (&v)[32]) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], v[c]);
+          for (int c = 0; c < 32; c += 2) mx8[(c >> 1) & 7] = fmax3(mx8[(c >> 1) & 7], v[c], v[c + 1]);
         };
         tc05::ld_32x32b_x32(s_self, va);
         tc05::ld_32x32b_x32(s_self + 32, vb);
@@ -474,18 +525,31 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           m = tmax;
         }
         const float mu = m == -INFINITY ? 0.f : m;
-        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // p = 2^(s*scale - m) for pairs of keys: the argument by one packed FMA, the
+        // exponential on the SFU or (pairs selected by kPolyMask) by exp2_poly2, the row sum by
+        // packed adds into four accumulators
+        const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
+        const uint64_t negmu2 = f2_pack(-mu, -mu);
+        uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};
         auto exp_chunk = [&](const float (&x)[32], int group) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             float pk[8];
 #pragma unroll
             for (int c = 0; c < 16; c += 2) {
-              const float p0 = fast_exp2(fmaf(x[16 * hh + c], a.scale_log2, -mu));
-              const float p1 = fast_exp2(fmaf(x[16 * hh + c + 1], a.scale_log2, -mu));
-              rs8[c & 7] += p0;
-              rs8[(c + 1) & 7] += p1;
-              pk[c >> 1] = __uint_as_float(MmaOp<T>::pack(p0, p1));
+              const int pi = c >> 1;
+              const uint64_t arg = f2_fma(f2_pack(x[16 * hh + c], x[16 * hh + c + 1]), scale2, negmu2);
+              float p0, p1;
+              if ((kPolyMask >> pi) & 1u) {
+                exp2_poly2(arg, p0, p1);
+              } else {
+                float a0, a1;
+                f2_unpack(arg, a0, a1);
+                p0 = fast_exp2(a0);
+                p1 = fast_exp2(a1);
+              }
+              rs2[pi & 3] = f2_add(rs2[pi & 3], f2_pack(p0, p1));
+              pk[pi] = __uint_as_float(MmaOp<T>::pack(p0, p1));
             }
             tc05::st_32x32b_x8(s_self + 64 + group * 16 + hh * 8, pk);
           }
@@ -499,8 +563,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         mask_chunk(vb, 1);
         exp_chunk(va, 2);
         exp_chunk(vb, 3);
-        const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) +
-                         ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        float rsl[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f2_unpack(rs2[k], rsl[2 * k], rsl[2 * k + 1]);
+        const float rs = ((rsl[0] + rsl[1]) + (rsl[2] + rsl[3])) + ((rsl[4] + rsl[5]) + (rsl[6] + rsl[7]));
         l = l * alpha + rs;
         // PV_w(j - 1), the last MMA into O_w, was issued before S_w(j) and is covered by the
         // commit that signalled S_w(j)
@@ -591,14 +657,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 
 // Host side: the plan kernel counts items in pairs of query tiles (launch_prefill_plan with
 // tq = 2 * TQ; PrefillArgs.tq stays TQ), max_work = num_tokens / (2 * TQ) + num_seqs.
-template <typename T, int D>
+template <typename T, int D, uint32_t kPolyMask>
 static cudaError_t launch_prefill_q2_t(const CUtensorMap& qm, const CUtensorMap& km,
                                        const CUtensorMap& vm, const PrefillArgs& a,
                                        int max_items, int num_sms, cudaStream_t stream) {
   constexpr SmemLayout L = q2_layout<D>();
   const int smem = static_cast<int>(L.total) + 1024;
   static bool configured = false;
-  auto kern = prefill_q2_kernel<T, D>;
+  auto kern = prefill_q2_kernel<T, D, kPolyMask>;
   if (!configured) {
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
@@ -619,19 +685,35 @@ static cudaError_t launch_prefill_q2_t(const CUtensorMap& qm, const CUtensorMap&
   return cudaGetLastError();
 }
 
+template <typename T, int D>
+static cudaError_t launch_prefill_q2_mode(int poly_mode, const CUtensorMap& qm,
+                                          const CUtensorMap& km, const CUtensorMap& vm,
+                                          const PrefillArgs& a, int max_items, int num_sms,
+                                          cudaStream_t stream) {
+  switch (poly_mode) {
+    case 0: return launch_prefill_q2_t<T, D, 0x00u>(qm, km, vm, a, max_items, num_sms, stream);
+    case 2: return launch_prefill_q2_t<T, D, 0xAAu>(qm, km, vm, a, max_items, num_sms, stream);
+    default: return launch_prefill_q2_t<T, D, 0x88u>(qm, km, vm, a, max_items, num_sms, stream);
+  }
+}
+
 cudaError_t launch_prefill_q2(int dtype, int head_dim, const CUtensorMap& qm,
                               const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
-                              int max_items, int num_sms, cudaStream_t stream) {
+                              int max_items, int num_sms, int poly_mode, cudaStream_t stream) {
   if (dtype == B200_DTYPE_BF16) {
     if (head_dim == 128)
-      return launch_prefill_q2_t<__nv_bfloat16, 128>(qm, km, vm, a, max_items, num_sms, stream);
+      return launch_prefill_q2_mode<__nv_bfloat16, 128>(poly_mode, qm, km, vm, a, max_items,
+                                                        num_sms, stream);
     if (head_dim == 64)
-      return launch_prefill_q2_t<__nv_bfloat16, 64>(qm, km, vm, a, max_items, num_sms, stream);
+      return launch_prefill_q2_mode<__nv_bfloat16, 64>(poly_mode, qm, km, vm, a, max_items,
+                                                       num_sms, stream);
   } else if (dtype == B200_DTYPE_F16) {
     if (head_dim == 128)
-      return launch_prefill_q2_t<__half, 128>(qm, km, vm, a, max_items, num_sms, stream);
+      return launch_prefill_q2_mode<__half, 128>(poly_mode, qm, km, vm, a, max_items, num_sms,
+                                                 stream);
     if (head_dim == 64)
-      return launch_prefill_q2_t<__half, 64>(qm, km, vm, a, max_items, num_sms, stream);
+      return launch_prefill_q2_mode<__half, 64>(poly_mode, qm, km, vm, a, max_items, num_sms,
+                                                stream);
   }
   return cudaErrorInvalidValue;
 }

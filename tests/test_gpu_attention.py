@@ -235,6 +235,23 @@ def test_prefill_tcgen05_f16_and_agrees_with_cuda_cores(pkg, oracle, ops):
     assert np.abs(tc - cc).max() <= BF16_ABS
 
 
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_prefill_poly_exp_modes(pkg, oracle, ops, mode):
+    """The two-tile kernel with none, a quarter or half of its softmax exponentials computed by
+    the cubic on the FMA pipe: same bf16 bound against the oracle (ragged chunks on prefixes,
+    GQA 4, D 128 and D 64)."""
+    lib = pkg._native.lib()
+    lib.b200_set_prefill_poly_exp(mode)
+    try:
+        for hd, seed in ((128, 31), (64, 32)):
+            b = pkg.workloads.custom(seed=seed, context_lens=[700, 129, 1, 260, 2000],
+                                     new_token_counts=[300, 129, 1, 77, 513], num_query_heads=32,
+                                     num_kv_heads=8, head_dim=hd, block_size=16)
+            _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=seed)
+    finally:
+        lib.b200_set_prefill_poly_exp(1)  # the default
+
+
 @pytest.mark.parametrize("two_tiles", [False, True])
 def test_prefill_config3_subset(pkg, oracle, ops, two_tiles):
     """4 of config 3's prefill chunks (on their cached prefixes) packed with 16 of its decodes."""
