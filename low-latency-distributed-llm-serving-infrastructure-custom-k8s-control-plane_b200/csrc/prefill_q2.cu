@@ -36,11 +36,13 @@ namespace b200 {
 namespace {
 
 constexpr int kBN = 128;
-__device__ constexpr uint32_t kPChunk[4] = {2, 3, 0, 1};
 constexpr int kKStages = 2;
 constexpr int kVStages = 2;
-constexpr uint32_t kRegsSoftmax = 176;
-constexpr uint32_t kRegsOther = 136;
+// Register split (setmaxnreg): each softmax thread holds its whole 128-column S row in registers
+// (one TMEM wait per tile); 256 x kRegsSoftmax + 128 x kRegsOther = 384 x 168, the registers the
+// CTA is launched with (the launcher checks the compiled count before the first launch).
+constexpr uint32_t kRegsSoftmax = 200;
+constexpr uint32_t kRegsOther = 104;
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;
 
 struct SmemLayout {
@@ -233,225 +235,227 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   tc05::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const int total = a.hdr->total_items;
-  if (warp >= 8)
+  // Each warpgroup changes its register count inside its own branch, so that the compiler
+  // allocates the softmax code against kRegsSoftmax and the producer / MMA code against
+  // kRegsOther.
+  if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
-  else
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-
-  if (warp == kWarpK || warp == kWarpV) {
-    // ------------------------------------------------------------------ TMA producers
-    {
-      const bool leader = elect_one_sync();
-      const bool is_k = warp == kWarpK;
-      const CUtensorMap* map = is_k ? &kmap : &vmap;
-      const uint32_t nst = is_k ? kKStages : kVStages;
-      uint64_t* full = &bars[is_k ? kBarKFull : kBarVFull];
-      uint64_t* empty = &bars[is_k ? kBarKEmpty : kBarVEmpty];
-      uint8_t* ring = smem + (is_k ? L.k0 : L.v0);
-      if (leader) {
-        if (is_k) prefetch_tensormap(&qmap);
-        prefetch_tensormap(map);
-      }
-      const int32_t layer_base = a.layer * a.nb;
-      uint32_t n_items = 0, kv_it = 0, q_issued = 0;
-      for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
-        const Q2Item it = q2_decode(a, item);
-        if (is_k) {
-          if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
-          ++q_issued;
-          if (leader) {
-            // both tiles, always: rows past the batch read the fill value, rows of the next
-            // sequence are never stored (their t >= n_q)
-            mbar_arrive_expect_tx(&bars[kBarQFull], 2 * QT);
-            for (int w = 0; w < 2; ++w)
-              for (int g = 0; g < a.group; ++g)
-#pragma unroll
-                for (int sub = 0; sub < SUB; ++sub)
-                  tc05::tma_load_4d(smem + L.q + w * QT + sub * 16384 + g * a.tq * 128, &qmap,
-                                    &bars[kBarQFull], 0, sub, it.h * a.group + g,
-                                    it.q_row0 + w * a.tq);
-          }
-        }
-        const int32_t* bt_row = a.bt + static_cast<int64_t>(it.s) * a.bt_stride;
-        const int n_kv = it.n_kv_all;
-        const int kv_end = it.kv_end_all;
-        bool ok = true;
-        int fb = 0, fw = 0;
-        int32_t nrow[kChunks];
-        auto fetch_rows = [&](int jj) {
-#pragma unroll
-          for (int b = 0; b < kChunks; ++b) {
-            const bool real = jj * kBN + 16 * b < kv_end;
-            int32_t blk = bt_row[real ? fb : 0];
-            if (blk < 0 || blk >= a.nb) {
-              if (leader) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
-              blk = 0;
-            }
-            nrow[b] = (layer_base + blk) * a.bs + (real ? fw : 0);
-            fw += 16;
-            if (fw == a.bs) {
-              fw = 0;
-              ++fb;
-            }
-          }
-        };
-        fetch_rows(0);
-        for (int j = 0; j < n_kv; ++j, ++kv_it) {
-          const uint32_t st = kv_it % nst;
-          const uint32_t ph = ((kv_it / nst) & 1u) ^ 1u;
-          int32_t rows[kChunks];
-#pragma unroll
-          for (int b = 0; b < kChunks; ++b) rows[b] = nrow[b];
-          if (j + 1 < n_kv) fetch_rows(j + 1);
-          if (!wait_or_abort(&empty[st], ph, abort_flag, a.status)) {
-            ok = false;
-            break;
-          }
-          if (leader) {
-            mbar_arrive_expect_tx(&full[st], KT);
-            uint8_t* dst = ring + st * KT;
-#pragma unroll
-            for (int b = 0; b < kChunks; ++b)
-#pragma unroll
-              for (int sub = 0; sub < SUB; ++sub)
-                tma_load_3d(dst + sub * (kBN * 128) + b * 2048, map, &full[st], 0,
-                            it.h * SUB + sub, rows[b]);
-          }
-        }
-        if (!ok) break;
-        ++n_items;
-      }
-      for (uint32_t f = kv_it > nst ? kv_it - nst : 0; f < kv_it; ++f)
-        mbar_wait_bounded(&full[f % nst], (f / nst) & 1u);
-      if (q_issued > 0) mbar_wait_bounded(&bars[kBarQFull], (q_issued - 1) & 1u);
-    }
-    __syncwarp();
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------------ MMA issuer
-    {
-      const bool leader = elect_one_sync();
-      uint32_t n_items = 0, kv_it = 0;
-      uint32_t c_tile[2] = {0u, 0u};  // tiles issued to warpgroup w so far (phase index)
-      constexpr uint32_t kHi = tc05::desc_hi_sw128(1024);
-      const uint32_t q_lo0 = tc05::desc_lo(base + L.q, 16);
-      const uint32_t k_lo0 = tc05::desc_lo(base + L.k0, 16);
-      const uint32_t v_lo0 = tc05::desc_lo(base + L.v0, kBN * 128);
-      auto issue_s = [&](uint32_t wg, uint32_t stage) {
-        const uint32_t q_lo = q_lo0 + wg * (QT >> 4);
-        const uint32_t k_lo = k_lo0 + stage * (KT >> 4);
-        const uint32_t d = tmem + wg * kBN;
-        if (!leader) return;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
-          const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
-          tc05::mma_f16(d, tc05::desc_join(q_lo + qo, kHi), tc05::desc_join(k_lo + ko, kHi),
-                        idesc_s, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](uint32_t stage, uint32_t wg, bool acc) {
-        const uint32_t v_lo = v_lo0 + stage * (KT >> 4);
-        const uint32_t p_t = tmem + wg * kBN + 64;
-        const uint32_t d = tmem + kColO + wg * D;
-        if (!leader) return;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t vrow16 = kPChunk[kk >> 1] * 2 + (kk & 1);
-          tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + vrow16 * (2048 >> 4), kHi),
-                           idesc_o, (acc || kk > 0) ? 1u : 0u);
-        }
-      };
-      auto wait_k = [&](uint32_t f) {
-        return wait_or_abort(&bars[kBarKFull + f % kKStages], (f / kKStages) & 1u, abort_flag,
-                             a.status);
-      };
-      bool ok = true;
-      for (int round = 0, item = snake_item(0); item < total && ok; item = snake_item(++round)) {
-        const Q2Item it = q2_decode(a, item);
-        const int n_kv = it.n_kv_all;
-        const int zw = q2_zero_wg(it);
-        const bool needs_zero = it.kv_end_all < n_kv * kBN;
-        if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
-        tc05::fence_after_sync();
-        // prologue: S_w(0) of this item (it may overlap the previous item's epilogues: S/P_w is
-        // free once PV_w of the previous item's last tile was issued, which came before)
-        if (!wait_k(kv_it)) break;
-        tc05::fence_after_sync();
-#pragma unroll
-        for (uint32_t w = 0; w < 2; ++w) {
-          if (it.n_kv[w] == 0) continue;
-          issue_s(w, kv_it % kKStages);
-          if (leader) tc05::commit(&bars[kBarSFull + w]);
-        }
+    if (warp == kWarpK || warp == kWarpV) {
+      // ------------------------------------------------------------------ TMA producers
+      {
+        const bool leader = elect_one_sync();
+        const bool is_k = warp == kWarpK;
+        const CUtensorMap* map = is_k ? &kmap : &vmap;
+        const uint32_t nst = is_k ? kKStages : kVStages;
+        uint64_t* full = &bars[is_k ? kBarKFull : kBarVFull];
+        uint64_t* empty = &bars[is_k ? kBarKEmpty : kBarVEmpty];
+        uint8_t* ring = smem + (is_k ? L.k0 : L.v0);
         if (leader) {
-          tc05::commit(&bars[kBarKEmpty + kv_it % kKStages]);
-          if (n_kv == 1) tc05::commit(&bars[kBarQEmpty]);
+          if (is_k) prefetch_tensormap(&qmap);
+          prefetch_tensormap(map);
         }
-        // each warpgroup's previous epilogue must have read O_w before PV_w(0) overwrites it;
-        // then the warpgroup may begin this item
-#pragma unroll
-        for (uint32_t w = 0; w < 2; ++w) {
-          if (!ok) break;
-          ok = wait_or_abort(&bars[kBarOEmpty + w], (n_items & 1u) ^ 1u, abort_flag, a.status);
-          if (ok && leader) tc05::mbar_arrive(&bars[kBarBegin + w]);
-        }
-        if (!ok) break;
-        tc05::fence_after_sync();
-        for (int j = 0; j < n_kv && ok; ++j) {
-          const uint32_t f = kv_it + j;
-          const bool zero_here = needs_zero && j == n_kv - 1;
-          if (!wait_or_abort(&bars[kBarVFull + f % kVStages], (f / kVStages) & 1u, abort_flag,
-                             a.status)) {
-            ok = false;
-            break;
+        const int32_t layer_base = a.layer * a.nb;
+        uint32_t n_items = 0, kv_it = 0, q_issued = 0;
+        for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
+          const Q2Item it = q2_decode(a, item);
+          if (is_k) {
+            if (!wait_or_abort(&bars[kBarQEmpty], (n_items & 1u) ^ 1u, abort_flag, a.status)) break;
+            ++q_issued;
+            if (leader) {
+              // both tiles, always: rows past the batch read the fill value, rows of the next
+              // sequence are never stored (their t >= n_q)
+              mbar_arrive_expect_tx(&bars[kBarQFull], 2 * QT);
+              for (int w = 0; w < 2; ++w)
+                for (int g = 0; g < a.group; ++g)
+  #pragma unroll
+                  for (int sub = 0; sub < SUB; ++sub)
+                    tc05::tma_load_4d(smem + L.q + w * QT + sub * 16384 + g * a.tq * 128, &qmap,
+                                      &bars[kBarQFull], 0, sub, it.h * a.group + g,
+                                      it.q_row0 + w * a.tq);
+            }
           }
-          if (zero_here && !wait_or_abort(&bars[kBarPFull + zw], ((zw ? c_tile[1] : c_tile[0]) + j) & 1u,
-                                          abort_flag, a.status)) {
-            ok = false;
-            break;
-          }
-#pragma unroll
-          for (uint32_t w = 0; w < 2; ++w) {
-            if (j >= it.n_kv[w]) continue;
-            if (!wait_or_abort(&bars[kBarPFull + w], (c_tile[w] + j) & 1u, abort_flag, a.status)) {
+          const int32_t* bt_row = a.bt + static_cast<int64_t>(it.s) * a.bt_stride;
+          const int n_kv = it.n_kv_all;
+          const int kv_end = it.kv_end_all;
+          bool ok = true;
+          int fb = 0, fw = 0;
+          int32_t nrow[kChunks];
+          auto fetch_rows = [&](int jj) {
+  #pragma unroll
+            for (int b = 0; b < kChunks; ++b) {
+              const bool real = jj * kBN + 16 * b < kv_end;
+              int32_t blk = bt_row[real ? fb : 0];
+              if (blk < 0 || blk >= a.nb) {
+                if (leader) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+                blk = 0;
+              }
+              nrow[b] = (layer_base + blk) * a.bs + (real ? fw : 0);
+              fw += 16;
+              if (fw == a.bs) {
+                fw = 0;
+                ++fb;
+              }
+            }
+          };
+          fetch_rows(0);
+          for (int j = 0; j < n_kv; ++j, ++kv_it) {
+            const uint32_t st = kv_it % nst;
+            const uint32_t ph = ((kv_it / nst) & 1u) ^ 1u;
+            int32_t rows[kChunks];
+  #pragma unroll
+            for (int b = 0; b < kChunks; ++b) rows[b] = nrow[b];
+            if (j + 1 < n_kv) fetch_rows(j + 1);
+            if (!wait_or_abort(&empty[st], ph, abort_flag, a.status)) {
               ok = false;
               break;
             }
-            tc05::fence_after_sync();
-            issue_pv(f % kVStages, w, j > 0);
-            if (leader) tc05::commit(&bars[kBarPvDone + w]);
-            if (j + 1 < it.n_kv[w]) {
-              // the first warpgroup needing K tile j+1 waits for it; the last releases it
-              const bool first = (w == 0) || (j + 1 >= it.n_kv[0]);
-              const bool last = (w == 1) || (j + 1 >= it.n_kv[1]);
-              if (first && !wait_k(f + 1)) {
+            if (leader) {
+              mbar_arrive_expect_tx(&full[st], KT);
+              uint8_t* dst = ring + st * KT;
+  #pragma unroll
+              for (int b = 0; b < kChunks; ++b)
+  #pragma unroll
+                for (int sub = 0; sub < SUB; ++sub)
+                  tma_load_3d(dst + sub * (kBN * 128) + b * 2048, map, &full[st], 0,
+                              it.h * SUB + sub, rows[b]);
+            }
+          }
+          if (!ok) break;
+          ++n_items;
+        }
+        for (uint32_t f = kv_it > nst ? kv_it - nst : 0; f < kv_it; ++f)
+          mbar_wait_bounded(&full[f % nst], (f / nst) & 1u);
+        if (q_issued > 0) mbar_wait_bounded(&bars[kBarQFull], (q_issued - 1) & 1u);
+      }
+      __syncwarp();
+    } else if (warp == kWarpMma) {
+      // ------------------------------------------------------------------ MMA issuer
+      {
+        const bool leader = elect_one_sync();
+        uint32_t n_items = 0, kv_it = 0;
+        uint32_t c_tile[2] = {0u, 0u};  // tiles issued to warpgroup w so far (phase index)
+        constexpr uint32_t kHi = tc05::desc_hi_sw128(1024);
+        const uint32_t q_lo0 = tc05::desc_lo(base + L.q, 16);
+        const uint32_t k_lo0 = tc05::desc_lo(base + L.k0, 16);
+        const uint32_t v_lo0 = tc05::desc_lo(base + L.v0, kBN * 128);
+        auto issue_s = [&](uint32_t wg, uint32_t stage) {
+          const uint32_t q_lo = q_lo0 + wg * (QT >> 4);
+          const uint32_t k_lo = k_lo0 + stage * (KT >> 4);
+          const uint32_t d = tmem + wg * kBN;
+          if (!leader) return;
+  #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+            const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
+            tc05::mma_f16(d, tc05::desc_join(q_lo + qo, kHi), tc05::desc_join(k_lo + ko, kHi),
+                          idesc_s, kk > 0 ? 1u : 0u);
+          }
+        };
+        auto issue_pv = [&](uint32_t stage, uint32_t wg, bool acc) {
+          const uint32_t v_lo = v_lo0 + stage * (KT >> 4);
+          const uint32_t p_t = tmem + wg * kBN + 64;
+          const uint32_t d = tmem + kColO + wg * D;
+          if (!leader) return;
+  #pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint32_t vrow16 = kk;  // P columns hold the keys in order: 16 keys per K step
+            tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + vrow16 * (2048 >> 4), kHi),
+                             idesc_o, (acc || kk > 0) ? 1u : 0u);
+          }
+        };
+        auto wait_k = [&](uint32_t f) {
+          return wait_or_abort(&bars[kBarKFull + f % kKStages], (f / kKStages) & 1u, abort_flag,
+                               a.status);
+        };
+        bool ok = true;
+        for (int round = 0, item = snake_item(0); item < total && ok; item = snake_item(++round)) {
+          const Q2Item it = q2_decode(a, item);
+          const int n_kv = it.n_kv_all;
+          const int zw = q2_zero_wg(it);
+          const bool needs_zero = it.kv_end_all < n_kv * kBN;
+          if (!wait_or_abort(&bars[kBarQFull], n_items & 1u, abort_flag, a.status)) break;
+          tc05::fence_after_sync();
+          // prologue: S_w(0) of this item (it may overlap the previous item's epilogues: S/P_w is
+          // free once PV_w of the previous item's last tile was issued, which came before)
+          if (!wait_k(kv_it)) break;
+          tc05::fence_after_sync();
+  #pragma unroll
+          for (uint32_t w = 0; w < 2; ++w) {
+            if (it.n_kv[w] == 0) continue;
+            issue_s(w, kv_it % kKStages);
+            if (leader) tc05::commit(&bars[kBarSFull + w]);
+          }
+          if (leader) {
+            tc05::commit(&bars[kBarKEmpty + kv_it % kKStages]);
+            if (n_kv == 1) tc05::commit(&bars[kBarQEmpty]);
+          }
+          // each warpgroup's previous epilogue must have read O_w before PV_w(0) overwrites it;
+          // then the warpgroup may begin this item
+  #pragma unroll
+          for (uint32_t w = 0; w < 2; ++w) {
+            if (!ok) break;
+            ok = wait_or_abort(&bars[kBarOEmpty + w], (n_items & 1u) ^ 1u, abort_flag, a.status);
+            if (ok && leader) tc05::mbar_arrive(&bars[kBarBegin + w]);
+          }
+          if (!ok) break;
+          tc05::fence_after_sync();
+          for (int j = 0; j < n_kv && ok; ++j) {
+            const uint32_t f = kv_it + j;
+            const bool zero_here = needs_zero && j == n_kv - 1;
+            if (!wait_or_abort(&bars[kBarVFull + f % kVStages], (f / kVStages) & 1u, abort_flag,
+                               a.status)) {
+              ok = false;
+              break;
+            }
+            if (zero_here && !wait_or_abort(&bars[kBarPFull + zw], ((zw ? c_tile[1] : c_tile[0]) + j) & 1u,
+                                            abort_flag, a.status)) {
+              ok = false;
+              break;
+            }
+  #pragma unroll
+            for (uint32_t w = 0; w < 2; ++w) {
+              if (j >= it.n_kv[w]) continue;
+              if (!wait_or_abort(&bars[kBarPFull + w], (c_tile[w] + j) & 1u, abort_flag, a.status)) {
                 ok = false;
                 break;
               }
               tc05::fence_after_sync();
-              issue_s(w, (f + 1) % kKStages);
-              if (leader) {
-                tc05::commit(&bars[kBarSFull + w]);
-                if (last) {
-                  tc05::commit(&bars[kBarKEmpty + (f + 1) % kKStages]);
-                  if (j + 1 == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);
+              issue_pv(f % kVStages, w, j > 0);
+              if (leader) tc05::commit(&bars[kBarPvDone + w]);
+              if (j + 1 < it.n_kv[w]) {
+                // the first warpgroup needing K tile j+1 waits for it; the last releases it
+                const bool first = (w == 0) || (j + 1 >= it.n_kv[0]);
+                const bool last = (w == 1) || (j + 1 >= it.n_kv[1]);
+                if (first && !wait_k(f + 1)) {
+                  ok = false;
+                  break;
+                }
+                tc05::fence_after_sync();
+                issue_s(w, (f + 1) % kKStages);
+                if (leader) {
+                  tc05::commit(&bars[kBarSFull + w]);
+                  if (last) {
+                    tc05::commit(&bars[kBarKEmpty + (f + 1) % kKStages]);
+                    if (j + 1 == n_kv - 1) tc05::commit(&bars[kBarQEmpty]);
+                  }
                 }
               }
             }
+            if (ok && leader) tc05::commit(&bars[kBarVEmpty + f % kVStages]);
           }
-          if (ok && leader) tc05::commit(&bars[kBarVEmpty + f % kVStages]);
+          if (!ok) break;
+          kv_it += n_kv;
+          c_tile[0] += it.n_kv[0];
+          c_tile[1] += it.n_kv[1];
+          ++n_items;
         }
-        if (!ok) break;
-        kv_it += n_kv;
-        c_tile[0] += it.n_kv[0];
-        c_tile[1] += it.n_kv[1];
-        ++n_items;
+        if (leader) tc05::commit(&bars[kBarFinal]);
+        mbar_wait_bounded(&bars[kBarFinal], 0);
       }
-      if (leader) tc05::commit(&bars[kBarFinal]);
-      mbar_wait_bounded(&bars[kBarFinal], 0);
+      __syncwarp();
     }
-    __syncwarp();
-  } else if (warp < 8) {
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // ------------------------------------------------------------------ softmax / epilogue
     const uint32_t wg = static_cast<uint32_t>(warp) >> 2;
     const int quarter = warp & 3;
@@ -485,7 +489,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         tc05::fence_after_sync();
         const bool need_mask = __any_sync(0xffffffffu, j * kBN + kBN - 1 > pos);
         const int lim = pos - j * kBN;
-        float va[32], vb[32];
+        // the whole S row of this thread: four 32-column loads, one wait
+        float sa[32], sb[32], sc[32], sd[32];
         auto mask_chunk = [&](float (&v)[32], int chunk) {
           if (need_mask) {
 #pragma unroll
@@ -500,20 +505,19 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; c += 2) mx8[(c >> 1) & 7] = fmax3(mx8[(c >> 1) & 7], v[c], v[c + 1]);
         };
-        tc05::ld_32x32b_x32(s_self, va);
-        tc05::ld_32x32b_x32(s_self + 32, vb);
+        tc05::ld_32x32b_x32(s_self, sa);
+        tc05::ld_32x32b_x32(s_self + 32, sb);
+        tc05::ld_32x32b_x32(s_self + 64, sc);
+        tc05::ld_32x32b_x32(s_self + 96, sd);
         tc05::wait_ld();
-        mask_chunk(va, 0);
-        mask_chunk(vb, 1);
-        max_chunk(va);
-        max_chunk(vb);
-        tc05::ld_32x32b_x32(s_self + 64, va);
-        tc05::ld_32x32b_x32(s_self + 96, vb);
-        tc05::wait_ld();
-        mask_chunk(va, 2);
-        mask_chunk(vb, 3);
-        max_chunk(va);
-        max_chunk(vb);
+        mask_chunk(sa, 0);
+        mask_chunk(sb, 1);
+        mask_chunk(sc, 2);
+        mask_chunk(sd, 3);
+        max_chunk(sa);
+        max_chunk(sb);
+        max_chunk(sc);
+        max_chunk(sd);
         const float smax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                  fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float tmax = smax * a.scale_log2;
@@ -554,15 +558,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             tc05::st_32x32b_x8(s_self + 64 + group * 16 + hh * 8, pk);
           }
         };
-        exp_chunk(va, 0);
-        exp_chunk(vb, 1);
-        tc05::ld_32x32b_x32(s_self, va);
-        tc05::ld_32x32b_x32(s_self + 32, vb);
-        tc05::wait_ld();
-        mask_chunk(va, 0);
-        mask_chunk(vb, 1);
-        exp_chunk(va, 2);
-        exp_chunk(vb, 3);
+        // P over the S columns 64..127, keys in order (all of S is in registers by now)
+        exp_chunk(sa, 0);
+        exp_chunk(sb, 1);
+        exp_chunk(sc, 2);
+        exp_chunk(sd, 3);
         float rsl[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) f2_unpack(rs2[k], rsl[2 * k], rsl[2 * k + 1]);
