@@ -456,9 +456,10 @@ def ours_arm(args):
         engine["tp_parity"] = None
     prefill = None
     if world == 1 and not args.no_prefill:
-        N.lib().b200_set_prefill_two_tiles(0 if args.prefill_one_tile else 1)
+        if args.prefill_kernel is not None:
+            N.lib().b200_set_prefill_kernel(args.prefill_kernel)
         prefill = prefill_measure(dev, 20, 3)
-        prefill["two_query_tiles"] = not args.prefill_one_tile
+        prefill["kernel_selector"] = args.prefill_kernel
     peak, peak_kind = load_peaks()
     ms_per_step = elapsed_ms / args.steps
     value = world * total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -519,7 +520,8 @@ def config3_arm(args):
     from llm_serving_b200 import paged_ops
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    pkg._native.lib().b200_set_prefill_two_tiles(0 if args.prefill_one_tile else 1)
+    if args.prefill_kernel is not None:
+        pkg._native.lib().b200_set_prefill_kernel(args.prefill_kernel)
     pkg._native.lib().b200_set_prefill_poly_exp(args.prefill_poly_exp)
     full = pkg.workloads.config3(seed=0)
     npre = 16
@@ -589,7 +591,8 @@ def config3_arm(args):
                                       "peak": peak, "unit": "TFLOP/s",
                                       "frac": round(tflops / peak, 4)}},
         "mixed_attention_tflops": round(attention_flops(full) / (ms_mix * 1e-3) / 1e12, 2),
-        "prefill_kernel": "one query tile per item" if args.prefill_one_tile else "two query tiles per item",
+        "prefill_kernel": {None: "library default", 0: "one query tile per item",
+                           1: "two query tiles per item", 2: "two streams per CTA"}[args.prefill_kernel],
         "prefill_poly_exp_mode": args.prefill_poly_exp,
         "device_status": paged_ops.read_status(dev),
     }
@@ -1285,9 +1288,10 @@ def main():
     ap.add_argument("--prefill-poly-exp", type=int, default=1, choices=[0, 1, 2],
                     help="config3: share of softmax exponentials on the FMA pipe (0 none, 1 a "
                          "quarter, 2 half)")
-    ap.add_argument("--prefill-one-tile", action="store_true",
-                    help="the one-query-tile prefill kernel instead of the default two-tile one "
-                         "(config3 and the prefill leg)")
+    ap.add_argument("--prefill-kernel", type=int, default=None, choices=[0, 1, 2],
+                    help="tensor-core prefill kernel (config3 and the prefill leg): 0 one query "
+                         "tile per item, 1 two tiles per item, 2 two streams per CTA; default: "
+                         "the library's")
     ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
                                            "meta"],
                     default="config2")

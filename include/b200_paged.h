@@ -192,10 +192,15 @@ int b200_paged_prefill(const B200PrefillParams* p, void* workspace, size_t works
  * (for A/B comparison); 0 restores the default. */
 void b200_set_prefill_cuda_cores(int32_t enable);
 
-/* Which tensor-core prefill kernel runs: nonzero (the default) = two query tiles per work item,
- * one per softmax warpgroup, each K/V tile staged once for both; 0 = one query tile per work item
- * with the K/V tiles alternating between the softmax warpgroups (kept for A/B comparison). */
-void b200_set_prefill_two_tiles(int32_t enable);
+/* Which tensor-core prefill kernel b200_paged_prefill runs (results agree within the bf16
+ * tolerance; a tuning and comparison knob):
+ *   0 = one query tile per work item, the K/V tiles alternating between the two softmax
+ *       warpgroups;
+ *   1 = two query tiles per work item, one per softmax warpgroup, each K/V tile staged once for
+ *       both (the default);
+ *   2 = two independent work streams per CTA, each with its own query tile, K/V rings, MMA warp
+ *       and softmax warpgroup, so one stream's item transitions overlap the other's work. */
+void b200_set_prefill_kernel(int32_t kernel);
 
 /* Share of the two-tile prefill's softmax exponentials computed by a cubic on the FMA pipe
  * instead of the SFU's ex2 (relative error below 7.5e-5 either way, far under bf16's): 0 = none,

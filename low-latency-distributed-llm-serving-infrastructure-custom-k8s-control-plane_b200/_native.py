@@ -87,7 +87,7 @@ SIGNATURES = [
     ("b200_paged_prefill_workspace_bytes", c_sz, [ctypes.POINTER(PrefillParams)]),
     ("b200_paged_prefill", ctypes.c_int, [ctypes.POINTER(PrefillParams), c_vp, c_sz, c_vp]),
     ("b200_set_prefill_cuda_cores", None, [c_i32]),
-    ("b200_set_prefill_two_tiles", None, [c_i32]),
+    ("b200_set_prefill_kernel", None, [c_i32]),
     ("b200_set_prefill_poly_exp", None, [c_i32]),
     ("b200_reshape_and_cache", ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp,
                                               ctypes.POINTER(CacheGeometry), c_i32, c_vp, c_i32,

@@ -131,7 +131,7 @@ int cache_tensor_map(const void* cache, const B200CacheGeometry& g, int box_rows
 // Process-wide tuning knobs (b200_set_decode_split_tokens, b200_set_prefill_cuda_cores).
 std::atomic<int> g_split_override{0};
 std::atomic<bool> g_force_cuda_core_prefill{false};
-std::atomic<bool> g_prefill_two_tiles{true};
+std::atomic<int> g_prefill_kernel{1};
 std::atomic<int> g_prefill_poly_exp{1};
 
 struct DecodePlan {
@@ -554,9 +554,11 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     if (rc != B200_OK) return rc;
     rc = cache_tensor_map(p.value_cache, p.geom, 16, &vm);
     if (rc != B200_OK) return rc;
-    // the two-tile kernel takes query tiles in pairs (the work list, sized for single tiles,
-    // holds the pairs as well)
-    const bool two_tiles = g_prefill_two_tiles.load(std::memory_order_relaxed);
+    // 0: one query tile per item (prefill.cu); 1: two tiles per item (prefill_q2.cu), which
+    // takes query tiles in pairs (the work list, sized for single tiles, holds the pairs as
+    // well); 2: two independent streams per CTA (prefill_ds.cu)
+    const int kernel = g_prefill_kernel.load(std::memory_order_relaxed);
+    const bool two_tiles = kernel == 1;
     b200::PrefillPlanArgs pa{};
     pa.cu_q = p.cu_seqlens;
     pa.ctx_lens = p.context_lens;
@@ -596,11 +598,16 @@ int b200_paged_prefill(const B200PrefillParams* pp, void* workspace, size_t work
     a.work = work;
     const int64_t max_items = pl.max_work * p.geom.num_kv_heads;
     const int items = static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30));
-    e = two_tiles ? b200::launch_prefill_q2(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items,
-                                            num_sms(),
-                                            g_prefill_poly_exp.load(std::memory_order_relaxed), st)
-                  : b200::launch_prefill_tc(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items,
-                                            num_sms(), st);
+    const int poly = g_prefill_poly_exp.load(std::memory_order_relaxed);
+    if (kernel == 2)
+      e = b200::launch_prefill_ds(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items, num_sms(),
+                                  poly, st);
+    else if (two_tiles)
+      e = b200::launch_prefill_q2(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items, num_sms(),
+                                  poly, st);
+    else
+      e = b200::launch_prefill_tc(p.geom.dtype, p.geom.head_dim, qm, km, vm, a, items, num_sms(),
+                                  st);
     if (e != cudaSuccess) return cuda_fail(e, "prefill");
     return B200_OK;
   }
@@ -637,8 +644,8 @@ void b200_set_prefill_poly_exp(int32_t mode) {
   g_prefill_poly_exp.store(mode < 0 || mode > 2 ? 1 : mode, std::memory_order_relaxed);
 }
 
-void b200_set_prefill_two_tiles(int32_t enable) {
-  g_prefill_two_tiles.store(enable != 0, std::memory_order_relaxed);
+void b200_set_prefill_kernel(int32_t kernel) {
+  g_prefill_kernel.store(kernel < 0 || kernel > 2 ? 1 : kernel, std::memory_order_relaxed);
 }
 
 void b200_set_prefill_cuda_cores(int32_t enable) {

@@ -155,6 +155,11 @@ cudaError_t launch_prefill_q2(int dtype, int head_dim, const CUtensorMap& qm,
                               const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
                               int max_items, int num_sms, int poly_mode, cudaStream_t stream);
 
+// Two independent work streams per CTA (prefill_ds.cu), items of one query tile each.
+cudaError_t launch_prefill_ds(int dtype, int head_dim, const CUtensorMap& qm,
+                              const CUtensorMap& km, const CUtensorMap& vm, const PrefillArgs& a,
+                              int max_items, int num_sms, int poly_mode, cudaStream_t stream);
+
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(int dtype, int head_dim, const CUtensorMap& km, const CUtensorMap& vm,
                              const DecodeArgs& a, int max_items, cudaStream_t stream);

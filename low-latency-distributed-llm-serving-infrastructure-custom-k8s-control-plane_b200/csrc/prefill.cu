@@ -110,12 +110,14 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, vol
 // clamped to the last bin (items that long are ordered among themselves arbitrarily).
 constexpr int kCostBins = 512;
 
-__device__ __forceinline__ int pair_cost(const PrefillPlanArgs& a, int s, int64_t count, int k) {
-  const int64_t tb = static_cast<int64_t>(k) * a.tq;
-  const int64_t n = count - tb < a.tq ? count - tb : a.tq;
-  const int64_t kv_end = a.ctx_lens[s] - count + tb + n;
-  const int64_t c = (kv_end + kBN - 1) / kBN;
-  return c < 0 ? 0 : (c >= kCostBins ? kCostBins - 1 : static_cast<int>(c));
+// (32-bit arithmetic: token counts and positions are below 2^31; kBN is a power of two)
+__device__ __forceinline__ int pair_cost(const PrefillPlanArgs& a, int s, int32_t count, int k) {
+  const int32_t tb = k * a.tq;
+  const int32_t n = count - tb < a.tq ? count - tb : a.tq;
+  const int32_t kv_end = a.ctx_lens[s] - count + tb + n;
+  const int32_t c = kv_end <= 0 ? 0 : ((kv_end + kBN - 1) >> 7);
+  static_assert(kBN == 128, "cost bins assume 128-key tiles");
+  return c >= kCostBins ? kCostBins - 1 : c;
 }
 
 __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
@@ -127,15 +129,17 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
   if (tid == 0) carry_s = 0;
   for (int b = tid; b < kCostBins; b += 1024) bins[b] = 0;
   __syncthreads();
-  auto items_of = [&](int s) -> int32_t {
-    const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
+  const uint32_t tq = static_cast<uint32_t>(a.tq);
+  auto count_of = [&](int s) -> int32_t { return static_cast<int32_t>(a.cu_q[s + 1] - a.cu_q[s]); };
+  auto items_of = [&](int32_t count) -> int32_t {
     return (count > 0 && !(a.skip_single && count == 1))
-               ? static_cast<int32_t>((count + a.tq - 1) / a.tq)
+               ? static_cast<int32_t>((static_cast<uint32_t>(count) + tq - 1) / tq)
                : 0;
   };
   for (int base = 0; base < a.S; base += 1024) {
     const int s = base + tid;
-    const int32_t n = s < a.S ? items_of(s) : 0;
+    const int32_t count = s < a.S ? count_of(s) : 0;
+    const int32_t n = items_of(count);
     int32_t v = n;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -158,7 +162,6 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
     const int32_t excl = incl - n;
     if (s < a.S) {
       if (sorted) {
-        const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
         for (int32_t k = 0; k < n; ++k) atomicAdd(&bins[pair_cost(a, s, count, k)], 1);
       } else {
         for (int32_t k = 0; k < n; ++k)
@@ -197,8 +200,8 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillPlanArgs a) {
     }
     __syncthreads();
     for (int s = tid; s < a.S; s += 1024) {
-      const int32_t n = items_of(s);
-      const int64_t count = a.cu_q[s + 1] - a.cu_q[s];
+      const int32_t count = count_of(s);
+      const int32_t n = items_of(count);
       for (int32_t k = 0; k < n; ++k) {
         const int32_t pos = atomicAdd(&bins[pair_cost(a, s, count, k)], 1);
         if (pos < a.max_work) a.work[pos] = make_int2(s, k);

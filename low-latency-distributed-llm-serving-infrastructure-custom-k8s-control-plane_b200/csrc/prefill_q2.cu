@@ -29,6 +29,7 @@
 #include <type_traits>
 
 #include "attention.cuh"
+#include "softmax_sm100.cuh"
 #include "tc05.cuh"
 
 namespace b200 {
@@ -88,55 +89,6 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, vol
   *abort_flag = 1;
   flag_status(status, B200_DEVICE_TIMEOUT);
   return false;
-}
-
-// ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of math) -----
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-// 2^x for both lanes of a packed pair on the FMA and integer pipes, leaving the SFU (whose ex2
-// throughput, shared by both softmax warpgroups, is what the softmax otherwise waits on) to the
-// other pairs.  x = j + f with j = round(x) -- adding 1.5 * 2^23 rounds to an integer held in the
-// low mantissa bits -- and f in [-0.5, 0.5]; 2^f comes from a cubic fitted here to 2^f on that
-// interval by relative least squares (maximum relative error 7.5e-5, against bf16's 2^-9), and j
-// is added to its exponent field.  Lanes are clamped to x >= -126 first, so masked (-inf) and
-// vanishing terms give a result of at most 2^-126 instead of a wrapped exponent.
-__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
-  float x0, x1;
-  f2_unpack(x2, x0, x1);
-  x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
-  const uint64_t t = f2_add(x2, f2_pack(12582912.f, 12582912.f));
-  const uint64_t r = f2_add(t, f2_pack(-12582912.f, -12582912.f));
-  const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), x2);
-  uint64_t p = f2_fma(f2_pack(0.0551716648f, 0.0551716648f), f, f2_pack(0.2426111251f, 0.2426111251f));
-  p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
-  p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
-  float t0, t1, q0, q1;
-  f2_unpack(t, t0, t1);
-  f2_unpack(p, q0, q1);
-  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
-  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
 // One work item: sequence s, KV head h, query tiles w = 0, 1 of TQ tokens starting at q_row0.
@@ -267,7 +219,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
               mbar_arrive_expect_tx(&bars[kBarQFull], 2 * QT);
               for (int w = 0; w < 2; ++w)
                 for (int g = 0; g < a.group; ++g)
-  #pragma unroll
+#pragma unroll
                   for (int sub = 0; sub < SUB; ++sub)
                     tc05::tma_load_4d(smem + L.q + w * QT + sub * 16384 + g * a.tq * 128, &qmap,
                                       &bars[kBarQFull], 0, sub, it.h * a.group + g,
@@ -281,7 +233,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           int fb = 0, fw = 0;
           int32_t nrow[kChunks];
           auto fetch_rows = [&](int jj) {
-  #pragma unroll
+#pragma unroll
             for (int b = 0; b < kChunks; ++b) {
               const bool real = jj * kBN + 16 * b < kv_end;
               int32_t blk = bt_row[real ? fb : 0];
@@ -302,7 +254,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             const uint32_t st = kv_it % nst;
             const uint32_t ph = ((kv_it / nst) & 1u) ^ 1u;
             int32_t rows[kChunks];
-  #pragma unroll
+#pragma unroll
             for (int b = 0; b < kChunks; ++b) rows[b] = nrow[b];
             if (j + 1 < n_kv) fetch_rows(j + 1);
             if (!wait_or_abort(&empty[st], ph, abort_flag, a.status)) {
@@ -312,9 +264,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
             if (leader) {
               mbar_arrive_expect_tx(&full[st], KT);
               uint8_t* dst = ring + st * KT;
-  #pragma unroll
+#pragma unroll
               for (int b = 0; b < kChunks; ++b)
-  #pragma unroll
+#pragma unroll
                 for (int sub = 0; sub < SUB; ++sub)
                   tma_load_3d(dst + sub * (kBN * 128) + b * 2048, map, &full[st], 0,
                               it.h * SUB + sub, rows[b]);
@@ -343,7 +295,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           const uint32_t k_lo = k_lo0 + stage * (KT >> 4);
           const uint32_t d = tmem + wg * kBN;
           if (!leader) return;
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t qo = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
             const uint32_t ko = static_cast<uint32_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
@@ -356,7 +308,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           const uint32_t p_t = tmem + wg * kBN + 64;
           const uint32_t d = tmem + kColO + wg * D;
           if (!leader) return;
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             const uint32_t vrow16 = kk;  // P columns hold the keys in order: 16 keys per K step
             tc05::mma_f16_ts(d, p_t + kk * 8, tc05::desc_join(v_lo + vrow16 * (2048 >> 4), kHi),
@@ -379,7 +331,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           // free once PV_w of the previous item's last tile was issued, which came before)
           if (!wait_k(kv_it)) break;
           tc05::fence_after_sync();
-  #pragma unroll
+#pragma unroll
           for (uint32_t w = 0; w < 2; ++w) {
             if (it.n_kv[w] == 0) continue;
             issue_s(w, kv_it % kKStages);
@@ -391,7 +343,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           }
           // each warpgroup's previous epilogue must have read O_w before PV_w(0) overwrites it;
           // then the warpgroup may begin this item
-  #pragma unroll
+#pragma unroll
           for (uint32_t w = 0; w < 2; ++w) {
             if (!ok) break;
             ok = wait_or_abort(&bars[kBarOEmpty + w], (n_items & 1u) ^ 1u, abort_flag, a.status);
@@ -412,7 +364,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
               ok = false;
               break;
             }
-  #pragma unroll
+#pragma unroll
             for (uint32_t w = 0; w < 2; ++w) {
               if (j >= it.n_kv[w]) continue;
               if (!wait_or_abort(&bars[kBarPFull + w], (c_tile[w] + j) & 1u, abort_flag, a.status)) {

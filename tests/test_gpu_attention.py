@@ -188,10 +188,10 @@ def test_prefill_mixed_bf16(pkg, oracle, ops):
     assert np.abs(out.float().cpu().numpy() - ref).max() <= BF16_ABS
 
 
-def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=True):
+def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, kernel=1):
     lib = pkg._native.lib()
     lib.b200_set_prefill_cuda_cores(1 if cuda_cores else 0)
-    lib.b200_set_prefill_two_tiles(1 if two_tiles else 0)
+    lib.b200_set_prefill_kernel(kernel)
     try:
         q, kc, vc, bt, ctx = device_batch(b, dtype, seed)
         cu = torch.from_numpy(b.cu_seqlens()).cuda()
@@ -207,7 +207,7 @@ def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=
         return got
     finally:
         lib.b200_set_prefill_cuda_cores(0)
-        lib.b200_set_prefill_two_tiles(1)  # the default
+        lib.b200_set_prefill_kernel(1)  # the default
 
 
 @pytest.mark.parametrize("hd,bs,hq,hkv,ctx,cnt", [
@@ -219,11 +219,11 @@ def _prefill_case(pkg, oracle, ops, b, dtype, seed, cuda_cores=False, two_tiles=
     (128, 16, 8, 8, [300, 129], [150, 129]),                                # MHA (128 tokens/tile)
     (128, 16, 32, 16, [260, 40], [260, 7]),                                 # GQA 2
 ])
-@pytest.mark.parametrize("two_tiles", [False, True])
-def test_prefill_tcgen05_parity(pkg, oracle, ops, hd, bs, hq, hkv, ctx, cnt, two_tiles):
+@pytest.mark.parametrize("kernel", [0, 1, 2])
+def test_prefill_tcgen05_parity(pkg, oracle, ops, hd, bs, hq, hkv, ctx, cnt, kernel):
     b = pkg.workloads.custom(seed=sum(cnt), context_lens=ctx, new_token_counts=cnt,
                              num_query_heads=hq, num_kv_heads=hkv, head_dim=hd, block_size=bs)
-    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd + hq, two_tiles=two_tiles)
+    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd + hq, kernel=kernel)
 
 
 def test_prefill_tcgen05_f16_and_agrees_with_cuda_cores(pkg, oracle, ops):
@@ -235,11 +235,12 @@ def test_prefill_tcgen05_f16_and_agrees_with_cuda_cores(pkg, oracle, ops):
     assert np.abs(tc - cc).max() <= BF16_ABS
 
 
+@pytest.mark.parametrize("kernel", [1, 2])
 @pytest.mark.parametrize("mode", [0, 1, 2])
-def test_prefill_poly_exp_modes(pkg, oracle, ops, mode):
-    """The two-tile kernel with none, a quarter or half of its softmax exponentials computed by
-    the cubic on the FMA pipe: same bf16 bound against the oracle (ragged chunks on prefixes,
-    GQA 4, D 128 and D 64)."""
+def test_prefill_poly_exp_modes(pkg, oracle, ops, mode, kernel):
+    """The two-tile and the dual-stream kernels with none, a quarter or half of their softmax
+    exponentials computed by the cubic on the FMA pipe: same bf16 bound against the oracle
+    (ragged chunks on prefixes, GQA 4, D 128 and D 64)."""
     lib = pkg._native.lib()
     lib.b200_set_prefill_poly_exp(mode)
     try:
@@ -247,20 +248,20 @@ def test_prefill_poly_exp_modes(pkg, oracle, ops, mode):
             b = pkg.workloads.custom(seed=seed, context_lens=[700, 129, 1, 260, 2000],
                                      new_token_counts=[300, 129, 1, 77, 513], num_query_heads=32,
                                      num_kv_heads=8, head_dim=hd, block_size=16)
-            _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=seed)
+            _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=seed, kernel=kernel)
     finally:
         lib.b200_set_prefill_poly_exp(1)  # the default
 
 
-@pytest.mark.parametrize("two_tiles", [False, True])
-def test_prefill_config3_subset(pkg, oracle, ops, two_tiles):
+@pytest.mark.parametrize("kernel", [0, 1, 2])
+def test_prefill_config3_subset(pkg, oracle, ops, kernel):
     """4 of config 3's prefill chunks (on their cached prefixes) packed with 16 of its decodes."""
     full = pkg.workloads.config3(seed=0)
     idx = [0, 1, 2, 3] + list(range(16, 32))
     b = pkg.workloads.custom(seed=3, context_lens=full.context_lens[idx],
                              new_token_counts=full.new_token_counts[idx], num_query_heads=32,
                              num_kv_heads=8, head_dim=128, block_size=16)
-    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=4, two_tiles=two_tiles)
+    _prefill_case(pkg, oracle, ops, b, torch.bfloat16, seed=4, kernel=kernel)
 
 
 def test_masked_kernel_random_masks(oracle, ops):
