@@ -181,6 +181,30 @@ class Scheduler:
 _GRAPH_BUCKETS = [1, 2, 4] + list(range(8, 257, 8)) + list(range(288, 2049, 32))
 
 
+def graph_decode_workspace_bytes(num_query_heads: int, key_cache: torch.Tensor,
+                                 value_cache: torch.Tensor, max_blocks_per_seq: int,
+                                 ctx_bound: int, max_rows: int, scale: float) -> int:
+    """Bytes of one decode workspace that serves every captured batch bucket up to `max_rows`
+    rows at the context bound.  The decode's split plan depends on the batch size -- a smaller
+    batch gets shorter splits so that every SM still has work -- so a bucket below the largest
+    can need more scratch than the largest one: the maximum over all buckets is taken.  Only
+    shapes and strides are read (no kernel runs), so this works on the host as well."""
+    L = N.lib()
+    D = key_cache.shape[-1]
+    dev = key_cache.device
+    q = torch.empty((max_rows, num_query_heads, D), dtype=key_cache.dtype, device=dev)
+    bt = torch.empty((max_rows, max_blocks_per_seq), dtype=torch.int32, device=dev)
+    ctx = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    need = 256
+    for rows in _GRAPH_BUCKETS:
+        if rows > max_rows:
+            break
+        p = paged_ops.decode_params(q[:rows], key_cache, value_cache, 0, bt[:rows], ctx[:rows],
+                                    scale, q[:rows], ctx_bound)
+        need = max(need, int(L.b200_paged_decode_workspace_bytes(ctypes.byref(p))))
+    return need
+
+
 class _DecodeGraph:
     """Static buffers and the captured graph of one decode bucket (``rows`` sequences)."""
 
@@ -350,20 +374,13 @@ class Engine:
 
     def _graph_workspace(self) -> torch.Tensor:
         """Decode workspace shared by every captured graph (graphs never run concurrently), sized
-        once for the largest bucket at the context bound so no capture ever reallocates it."""
+        once for every bucket at the context bound so no capture ever reallocates it."""
         if self._graph_ws is None:
-            L = N.lib()
-            kc = self.kv.key_cache
-            q = torch.empty((self._max_rows, self.model.hq, kc.shape[-1]), dtype=kc.dtype,
-                            device=self.device)
-            bt = torch.empty((self._max_rows, self.kv.pool.max_blocks_per_seq),
-                             dtype=torch.int32, device=self.device)
-            ctx = torch.empty(self._max_rows, dtype=torch.int32, device=self.device)
-            p = paged_ops.decode_params(q, kc, self.kv.value_cache, 0, bt, ctx, self.scale, q,
-                                        self._ctx_bound, None,
-                                        paged_ops.status_word(self.device))
-            need = int(L.b200_paged_decode_workspace_bytes(ctypes.byref(p)))
-            self._graph_ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+            need = graph_decode_workspace_bytes(self.model.hq, self.kv.key_cache,
+                                                self.kv.value_cache,
+                                                self.kv.pool.max_blocks_per_seq, self._ctx_bound,
+                                                self._max_rows, self.scale)
+            self._graph_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._graph_ws
 
     def _graph_decode(self, decodes: List[Sequence]) -> Optional[List[int]]:
