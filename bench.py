@@ -811,6 +811,32 @@ ENGINE5_MAX_OUT = 1024
 ENGINE5_MAX_LEN = 32768 + ENGINE5_MAX_OUT
 
 
+def engine5_workload(world, kv_gb, bs=16, seed=5):
+    """The config-5 request set at tensor-parallel size `world` (host only): the pool's block
+    count for `kv_gb` per GPU, running contexts U[8192, 32768] drawn until they would exceed 95 %
+    of it, their output lengths U[256, 1024], and a waiting queue of twice as many prompts
+    U[8192, 32768] with their output lengths.  Also returns the generator, which the engine leg
+    goes on drawing from (free-list shuffle, prompt token ids)."""
+    from llm_serving_b200.model import CONFIG5, kv_bytes_per_token
+    blocks = int(kv_gb * 1e9 // (kv_bytes_per_token(CONFIG5, world) * bs))
+    rng = np.random.default_rng(seed)
+    ctxs = []
+    used = 0
+    while True:
+        c = int(rng.integers(8192, 32769))
+        need = -(-c // bs)
+        if used + need > 0.95 * blocks:
+            break
+        ctxs.append(c)
+        used += need
+    out_lens = rng.integers(256, ENGINE5_MAX_OUT + 1, size=len(ctxs))
+    n_wait = 2 * len(ctxs)
+    wait_lens = rng.integers(8192, 32769, size=n_wait)
+    wait_outs = rng.integers(256, ENGINE5_MAX_OUT + 1, size=n_wait)
+    return {"blocks": blocks, "ctxs": ctxs, "out_lens": out_lens, "wait_lens": wait_lens,
+            "wait_outs": wait_outs, "rng": rng}
+
+
 def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
     """BASELINE config 5 under preemption pressure, tensor-parallel by KV head over the launched
     ranks (call on every rank, inside the process group when world > 1).
@@ -836,21 +862,11 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
     from llm_serving_b200.model import CONFIG5, kv_bytes_per_token
     shape = CONFIG5
     bs = 16
-    blocks = int(args.kv_gb * 1e9 // (kv_bytes_per_token(shape, world) * bs))
-    rng = np.random.default_rng(5)
-    ctxs = []
-    used = 0
-    while True:
-        c = int(rng.integers(8192, 32769))
-        need = -(-c // bs)
-        if used + need > 0.95 * blocks:
-            break
-        ctxs.append(c)
-        used += need
-    out_lens = rng.integers(256, ENGINE5_MAX_OUT + 1, size=len(ctxs))
-    n_wait = 2 * len(ctxs)
-    wait_lens = rng.integers(8192, 32769, size=n_wait)
-    wait_outs = rng.integers(256, ENGINE5_MAX_OUT + 1, size=n_wait)
+    w5 = engine5_workload(world, args.kv_gb, bs)
+    blocks, ctxs, out_lens = w5["blocks"], w5["ctxs"], w5["out_lens"]
+    wait_lens, wait_outs = w5["wait_lens"], w5["wait_outs"]
+    n_wait = len(wait_lens)
+    rng = w5["rng"]
     eng = build_engine(shape, total_blocks=blocks, block_size=bs, rank=rank, world=world,
                        device=dev, seed=0, max_batch_size=32 * world,
                        max_num_batched_tokens=ENGINE5_MAX_LEN * world,
