@@ -19,12 +19,17 @@
 // [256 + w*D, 256 + (w+1)*D).
 //
 // Per-item synchronisation: the MMA warp waits OEmpty_w (warpgroup w has read O_w of the previous
-// item) before the first PV_w of an item, then arrives Begin_w; the warpgroup waits Begin_w before
-// the item's softmax.  This keeps every warpgroup within one item of the MMA warp even when it has
-// no rows in some items (the last pair of a sequence may hold one tile), so every parity wait is
-// unambiguous.  V rows past the item's last key in its last tile are zeroed by the warpgroup that
-// owns that tile's latest rows (masked P is exactly 0, but 0 * NaN from an unwritten slot is not);
-// the MMA warp waits for that warpgroup's P before issuing either PV on the tile.
+// item) before the first PV_w of an item.  A warpgroup with rows in the item is gated by its first
+// SFull wait, and it cannot arrive OEmpty again before the MMA warp consumed the previous arrival
+// (that needs PV_w of this item); a warpgroup without rows in the item (the last pair of a sequence
+// may hold one tile) waits Begin_w instead, which the MMA warp arrives after that OEmpty_w wait.
+// So every parity wait is unambiguous.  V rows past the item's last key in its last tile are zeroed (masked P is exactly 0,
+// but 0 * NaN from an unwritten slot is not) by warpgroup 0 when it attends that tile (its softmax
+// runs first), else by warpgroup 1; the MMA warp waits for that warpgroup's P before issuing
+// either PV on the tile.
+// Epilogue: each softmax warp stages its 32 output rows, 64 columns at a time, in its own 4 KB of
+// shared memory (16-byte chunks XOR-swizzled by row), and writes them back as whole 128-byte row
+// segments, four rows per store instruction.
 // Every wait is bounded; an expired wait records B200_DEVICE_TIMEOUT and stops the CTA.
 #include <type_traits>
 
@@ -47,8 +52,11 @@ constexpr uint32_t kRegsOther = 104;
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;
 
 struct SmemLayout {
-  uint32_t q, k0, v0, bars, total;
+  uint32_t q, k0, v0, o, bars, total;
 };
+
+// epilogue staging: 32 rows x 128 bytes per softmax warp
+constexpr uint32_t kOStageWarp = 32 * 128;
 
 template <int D>
 __host__ __device__ constexpr SmemLayout q2_layout() {
@@ -56,7 +64,9 @@ __host__ __device__ constexpr SmemLayout q2_layout() {
   constexpr uint32_t QT = SUB * 128 * 128;  // one 128-row query tile
   constexpr uint32_t KT = SUB * kBN * 128;  // one 128-key K or V tile
   constexpr uint32_t KV = (kKStages + kVStages) * KT;
-  return SmemLayout{0, 2 * QT, 2 * QT + kKStages * KT, 2 * QT + KV, 2 * QT + KV + 512};
+  constexpr uint32_t OS = 8 * kOStageWarp;
+  return SmemLayout{0, 2 * QT, 2 * QT + kKStages * KT, 2 * QT + KV, 2 * QT + KV + OS,
+                    2 * QT + KV + OS + 512};
 }
 
 enum : int {
@@ -124,8 +134,11 @@ __device__ __forceinline__ Q2Item q2_decode(const PrefillArgs& a, int item) {
   return it;
 }
 
-// The warpgroup that owns the item's latest rows (it zeroes the V rows past kv_end_all).
-__device__ __forceinline__ int q2_zero_wg(const Q2Item& it) { return it.n_kv[1] > 0 ? 1 : 0; }
+// The warpgroup that zeroes the V rows past kv_end_all in the item's last KV tile: warpgroup 0
+// when it attends that tile, else warpgroup 1 (which then holds the item's latest rows).
+__device__ __forceinline__ int q2_zero_wg(const Q2Item& it) {
+  return it.n_kv[0] == it.n_kv_all ? 0 : 1;
+}
 
 }  // namespace
 
@@ -347,7 +360,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
           for (uint32_t w = 0; w < 2; ++w) {
             if (!ok) break;
             ok = wait_or_abort(&bars[kBarOEmpty + w], (n_items & 1u) ^ 1u, abort_flag, a.status);
-            if (ok && leader) tc05::mbar_arrive(&bars[kBarBegin + w]);
+            if (ok && leader && it.n_kv[w] == 0) tc05::mbar_arrive(&bars[kBarBegin + w]);
           }
           if (!ok) break;
           tc05::fence_after_sync();
@@ -418,17 +431,23 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     const uint32_t s_self = trow + wg * kBN;
     const uint32_t o_self = trow + kColO + wg * D;
     const int sm_tid = quarter * 32 + lane;
-    uint32_t c_tile = 0, kv_it = 0, n_items = 0;
+    uint32_t c_tile = 0, kv_it = 0, n_items = 0, n_idle = 0;
+    Q2Item nx{};
+    if (snake_item(0) < total) nx = q2_decode(a, snake_item(0));
     for (int round = 0, item = snake_item(0); item < total; item = snake_item(++round)) {
-      const Q2Item it = q2_decode(a, item);
+      const Q2Item it = nx;
       const int n_kv = wg ? it.n_kv[1] : it.n_kv[0];
       const int n_q = wg ? it.n_q[1] : it.n_q[0];
       const bool valid = t < n_q;
       const int pos = valid ? it.pos0 + static_cast<int>(wg) * a.tq + t : -1;
       const bool zeroer = static_cast<int>(wg) == q2_zero_wg(it) &&
                           it.kv_end_all < it.n_kv_all * kBN;
-      bool ok = wait_or_abort(&bars[kBarBegin + wg], n_items & 1u, abort_flag, a.status);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      bool ok = true;
+      if (n_kv == 0) {
+        ok = wait_or_abort(&bars[kBarBegin + wg], n_idle & 1u, abort_flag, a.status);
+        ++n_idle;
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
       float m = -INFINITY, l = 0.f;
       int j = 0;
       for (; j < n_kv; ++j) {
@@ -558,22 +577,27 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         if (lane == 0) tc05::mbar_arrive(&bars[kBarPFull + wg]);
       }
       if (!ok) break;
+      // the next item's indices load here, ahead of this item's output stores (loads issued after
+      // them queue behind them)
+      if (snake_item(round + 1) < total) nx = q2_decode(a, snake_item(round + 1));
       // ---- epilogue: this warpgroup's rows only
       if (n_kv > 0) {
         ok = wait_or_abort(&bars[kBarPvDone + wg], (c_tile + n_kv - 1) & 1u, abort_flag, a.status);
         if (!__all_sync(0xffffffffu, ok)) break;
         tc05::fence_after_sync();
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        T* orow = static_cast<T*>(a.out) +
-                  static_cast<int64_t>(it.q_row0 + static_cast<int>(wg) * a.tq + t) * a.o_stok +
-                  static_cast<int64_t>(it.h * a.group + g) * a.o_shead;
+        if (a.vec_out) {
+          // stage 64 columns of the warp's 32 rows, then write 4 rows x 128 B per instruction
+          uint8_t* stage = smem + L.o + warp * kOStageWarp;
+          const int64_t head0 = static_cast<int64_t>(it.h * a.group);
+          const int tok0 = it.q_row0 + static_cast<int>(wg) * a.tq;
 #pragma unroll
-        for (int ch = 0; ch < D / 16; ++ch) {
-          float o[16];
-          tc05::ld_32x32b_x16(o_self + ch * 16, o);
-          tc05::wait_ld();
-          if (valid) {
-            if (a.vec_out) {
+          for (int half = 0; half < D / 64; ++half) {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              float o[16];
+              tc05::ld_32x32b_x16(o_self + half * 64 + ch * 16, o);
+              tc05::wait_ld();
 #pragma unroll
               for (int c8 = 0; c8 < 2; ++c8) {
                 uint4 v;
@@ -581,9 +605,38 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                 v.y = MmaOp<T>::pack(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
                 v.z = MmaOp<T>::pack(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
                 v.w = MmaOp<T>::pack(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
-                *reinterpret_cast<uint4*>(orow + ch * 16 + c8 * 8) = v;
+                const int k = ch * 2 + c8;
+                *reinterpret_cast<uint4*>(stage + lane * 128 + ((k ^ (lane & 7)) << 4)) = v;
               }
-            } else {
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = i * 4 + (lane >> 3);  // row within the warp
+              const int k = lane & 7;              // 16-byte chunk within the 128-byte segment
+              const uint4 v =
+                  *reinterpret_cast<const uint4*>(stage + rr * 128 + ((k ^ (rr & 7)) << 4));
+              const int wrow = quarter * 32 + rr;  // row within the warpgroup's tile
+              const int gg = wrow / a.tq;
+              const int tt = wrow - gg * a.tq;
+              if (tt < n_q) {
+                T* dst = static_cast<T*>(a.out) + static_cast<int64_t>(tok0 + tt) * a.o_stok +
+                         (head0 + gg) * a.o_shead + half * 64 + k * 8;
+                *reinterpret_cast<uint4*>(dst) = v;
+              }
+            }
+            __syncwarp();
+          }
+        } else {
+          T* orow = static_cast<T*>(a.out) +
+                    static_cast<int64_t>(it.q_row0 + static_cast<int>(wg) * a.tq + t) * a.o_stok +
+                    static_cast<int64_t>(it.h * a.group + g) * a.o_shead;
+#pragma unroll
+          for (int ch = 0; ch < D / 16; ++ch) {
+            float o[16];
+            tc05::ld_32x32b_x16(o_self + ch * 16, o);
+            tc05::wait_ld();
+            if (valid) {
 #pragma unroll
               for (int c = 0; c < 16; ++c) orow[ch * 16 + c] = from_f32<T>(o[c] * inv);
             }
