@@ -171,7 +171,8 @@ class Sim:
         for n, it in enumerate(self.items):
             n_kv = it["n_kv_all"]
             nk = it["n_kv"]
-            zw = 1 if nk[1] > 0 else 0
+            # warpgroup 0 zeroes the V tail when it attends the item's last KV tile
+            zw = 0 if nk[0] == n_kv else 1
             needs_zero = it["kv_end_all"] < n_kv * KBN
             yield from self.wait(role, self.q_full, n)
             yield from self.wait(role, self.k_full[kv_it % K_STAGES], kv_it // K_STAGES)
@@ -186,12 +187,15 @@ class Sim:
             for w in (0, 1):
                 yield from self.wait(role, self.o_empty[w],
                                      n if self.mutation == "wrong_o_phase" else n - 1)
-                self.begin[w].arrive()
+                # only a warpgroup without rows in the item waits for Begin
+                if nk[w] == 0:
+                    self.begin[w].arrive()
             for j in range(n_kv):
                 f = kv_it + j
                 zero_here = needs_zero and j == n_kv - 1
                 yield from self.wait(role, self.v_full[f % V_STAGES], f // V_STAGES)
-                if zero_here and self.mutation != "no_zero_wait":
+                # (implied by the PFull waits below when warpgroup 0 zeroes; kept as in the kernel)
+                if zero_here:
                     yield from self.wait(role, self.p_full[zw], c[zw] + j)
                 for w in (0, 1):
                     if j >= nk[w]:
@@ -229,13 +233,19 @@ class Sim:
 
     def softmax_warp(self, w, quarter):
         role = f"SM{w}.{quarter}"
-        c, kv_it = 0, 0
+        c, kv_it, idle = 0, 0, 0
         for n, it in enumerate(self.items):
             n_kv = it["n_kv"][w]
-            zeroer = (w == (1 if it["n_kv"][1] > 0 else 0)) and \
-                it["kv_end_all"] < it["n_kv_all"] * KBN
-            if self.mutation != "no_begin":
-                yield from self.wait(role, self.begin[w], n)
+            zw = 0 if it["n_kv"][0] == it["n_kv_all"] else 1
+            if self.mutation == "wrong_zeroer":
+                # the warpgroup with the latest rows zeroes, while the MMA warp assumes the rule
+                zw = 1 if it["n_kv"][1] > 0 else 0
+            zeroer = w == zw and it["kv_end_all"] < it["n_kv_all"] * KBN
+            # a warpgroup with rows is gated by its first SFull wait; one without waits for Begin
+            if n_kv == 0 and self.mutation != "no_begin":
+                yield from self.wait(role, self.begin[w], idle)
+            if n_kv == 0:
+                idle += 1
             for j in range(n_kv):
                 yield from self.wait(role, self.s_full[w], c + j)
                 if self.s_tag[w] not in (("S", n, j), ("P", n, j)):
@@ -342,5 +352,5 @@ def check(trials=300, seed=0, mutation=None):
     return None
 
 
-MUTATIONS = ("no_zero_wait", "release_k_early", "wrong_o_phase", "no_begin", "s_before_pv",
+MUTATIONS = ("wrong_zeroer", "release_k_early", "wrong_o_phase", "no_begin", "s_before_pv",
              "no_empty_wait", "early_epilogue")
