@@ -807,6 +807,118 @@ def reference_engine4_arm(args):
     return 0
 
 
+def reference_engine5_arm(args):
+    """`--workload engine5 --impl reference`: the reference's own engine on one B200 on a bounded
+    config-5 sample.  The reference's LLMEngine + Scheduler + PagedKVCacheManager (app/, staged
+    unmodified into oracle/_ref) with its compiled allocator binding and CudaKVCacheStrategy, a
+    transformers Llama of the Llama-3-8B shape (random init, bf16) through its paged hook on the
+    SDPA path.  The running sequences of config 5 (contexts U[8192, 32768] at 95 % of a
+    `--kv-gb` pool, free list shuffled through the reference allocator, random K/V, placed as if
+    prefilled) are decoded for `--steps` timed steps after `--warmup` (at most 2) untimed ones,
+    within `--seconds`.  The waiting queue is left out: admitting one of its 8k-32k-token prompts
+    runs SDPA over a dense (prompt x context) mask with grouped heads, whose attention matrix
+    (32 heads x 32k x 32k fp32 = 137 GB at the longest prompt) does not fit next to the model and
+    the pool.  Compare with `--workload engine5 --decode-only` (this package's engine on the same
+    sample).  Rank 0 only."""
+    import glob
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    ref_parent = os.path.join(ROOT, "oracle", "_ref")
+    binding = glob.glob(os.path.join(ref_parent, "llm_allocator_cpp*.so"))
+    if not (os.path.isfile(os.path.join(ref_parent, "app", "engine", "llm_engine.py")) and binding):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference engine is not staged "
+                          "(make -C oracle ref, which needs a reference checkout)"}))
+        return 0
+    import torch
+    if not hasattr(torch.cuda, "_device_ctx"):   # see reference_engine4_arm
+        torch.cuda._device_ctx = torch.cuda.device
+    sys.path.insert(0, ref_parent)
+    import llm_allocator_cpp  # noqa: F401  (the compiled reference binding)
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from app.engine.llm_engine import LLMEngine
+    from app.memory.manager import PagedKVCacheManager
+    from app.scheduler.scheduler import Scheduler
+    from app.scheduler.sequence import Sequence, SequenceStatus
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from llm_serving_b200.model import CONFIG5 as shape
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    bs = 16
+    w5 = engine5_workload(1, args.kv_gb, bs)
+    blocks, ctxs, out_lens, rng = w5["blocks"], w5["ctxs"], w5["out_lens"], w5["rng"]
+    cfg = LlamaConfig(vocab_size=shape.vocab, hidden_size=shape.hidden,
+                      intermediate_size=shape.ffn, num_hidden_layers=shape.num_layers,
+                      num_attention_heads=shape.num_heads, num_key_value_heads=shape.num_kv_heads,
+                      head_dim=shape.head_dim, max_position_embeddings=ENGINE5_MAX_LEN,
+                      rms_norm_eps=shape.rms_eps, rope_theta=shape.rope_theta)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    kv = PagedKVCacheManager.from_model_config(cfg, total_blocks=blocks, block_size=bs,
+                                               dtype=torch.bfloat16, device=str(dev))
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    for t in (kv.key_cache, kv.value_cache):
+        t.normal_(generator=g)
+    sched = Scheduler(kv_cache_manager=kv, max_batch_size=32,
+                      max_num_batched_tokens=ENGINE5_MAX_LEN, block_size=bs,
+                      max_model_len=ENGINE5_MAX_LEN)
+    eng = LLMEngine(kv_cache_manager=kv, scheduler=sched, model=model)
+    # shuffled free list: filler sequences take the whole pool, released in random order
+    fillers = 64
+    per = blocks // fillers
+    fill = [Sequence(seq_id=-1 - f, prompt_token_ids=[1] * (per * bs), max_tokens=1)
+            for f in range(fillers)]
+    for f in fill:
+        kv.allocate_prefix_blocks(f)
+    for f in rng.permutation(fillers):
+        kv.free_sequence(fill[int(f)])
+    seqs = []
+    for c, o in zip(ctxs, out_lens):
+        s = eng.add_request(prompt_token_ids=[1] * c, max_tokens=int(o))
+        sched.waiting.remove(s)
+        kv.allocate_prefix_blocks(s)
+        s.output_token_ids.append(2)          # as if prefilled: the next step decodes
+        s.status = SequenceStatus.RUNNING
+        sched.running.append(s)
+        seqs.append(s)
+    for _ in range(max(1, min(args.warmup, 2))):
+        eng.step()
+    torch.cuda.synchronize(dev)
+    gen0 = sum(len(s.output_token_ids) for s in seqs)
+    steps = 0
+    t0 = time.perf_counter()
+    while steps < args.steps and time.perf_counter() - t0 < args.seconds:
+        eng.step()
+        steps += 1
+    torch.cuda.synchronize(dev)
+    elapsed = time.perf_counter() - t0
+    toks = sum(len(s.output_token_ids) for s in seqs) - gen0
+    value = toks / elapsed
+    line = {
+        "impl": "reference", "metric": "engine output tokens/s (config 5, decode-only sample)",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config5 decode-only sample: Llama-3-8B shape random init, bf16; "
+                               "the running contexts U[8192,32768] at 95% pool occupancy "
+                               "(shuffled free list), no waiting queue: every step decodes them "
+                               "all", "kv_pool_blocks": blocks, "sequences": len(ctxs),
+                   "sum_ctx": int(sum(ctxs)),
+                   "engine": "reference LLMEngine + Scheduler + PagedKVCacheManager "
+                             "(CudaKVCacheStrategy, compiled reference allocator), transformers "
+                             "Llama through the reference's paged hook (SDPA path), on the GPU"},
+        "output_tokens": toks, "elapsed_s": round(elapsed, 2),
+        "ms_per_step": round(elapsed * 1e3 / max(steps, 1), 1), "time_box_s": args.seconds,
+        "preemptions": sched.preemption_count,
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
 ENGINE5_MAX_OUT = 1024
 ENGINE5_MAX_LEN = 32768 + ENGINE5_MAX_OUT
 
@@ -837,7 +949,7 @@ def engine5_workload(world, kv_gb, bs=16, seed=5):
             "wait_outs": wait_outs, "rng": rng}
 
 
-def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
+def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False, queue=True):
     """BASELINE config 5 under preemption pressure, tensor-parallel by KV head over the launched
     ranks (call on every rank, inside the process group when world > 1).
 
@@ -851,7 +963,9 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
     block when none is free is preempted -- its blocks freed, itself re-queued at the front and
     later recomputed from its prompt and outputs.  The per-step token budget is
     `ENGINE5_MAX_LEN * world`, so every TP size admits the same work per rank (weak scaling: TP t
-    holds t times the sequences in the same bytes per GPU).
+    holds t times the sequences in the same bytes per GPU).  With `queue=False` the waiting queue
+    is left out: every step decodes the running sequences (the sample the reference's own engine
+    can run on one GPU, see reference_engine5_arm).
 
     Returns a dict (identical on every rank; times are the max over ranks)."""
     import torch
@@ -865,6 +979,8 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
     w5 = engine5_workload(world, args.kv_gb, bs)
     blocks, ctxs, out_lens = w5["blocks"], w5["ctxs"], w5["out_lens"]
     wait_lens, wait_outs = w5["wait_lens"], w5["wait_outs"]
+    if not queue:
+        wait_lens, wait_outs = wait_lens[:0], wait_outs[:0]
     n_wait = len(wait_lens)
     rng = w5["rng"]
     eng = build_engine(shape, total_blocks=blocks, block_size=bs, rank=rank, world=world,
@@ -936,11 +1052,14 @@ def run_engine5(args, world, rank, dev, steps, warmup, sample_clocks=False):
         "running_at_end": len(eng.scheduler.running), "waiting_at_end": len(eng.scheduler.waiting),
         "sum_ctx": int(sum(ctxs)), "kv_pool_blocks_per_gpu": blocks, "kv_gb_per_gpu": args.kv_gb,
         "wall_ms_max_over_ranks": round(wall_ms, 1),
-        "workload": "config5: Llama-3-8B shape random init, bf16, TP by KV head; running "
-                    "contexts U[8192,32768] at 95% pool occupancy (shuffled free list) + a queue "
-                    "of twice as many prompts U[8192,32768]; outputs U[256,1024]; reference "
-                    "admission and recompute-preemption policy; weak scaling (pool bytes per GPU "
-                    "fixed, TP t holds t x the sequences)",
+        "workload": ("config5: Llama-3-8B shape random init, bf16, TP by KV head; running "
+                     "contexts U[8192,32768] at 95% pool occupancy (shuffled free list) + a queue "
+                     "of twice as many prompts U[8192,32768]; outputs U[256,1024]; reference "
+                     "admission and recompute-preemption policy; weak scaling (pool bytes per GPU "
+                     "fixed, TP t holds t x the sequences)") if queue else
+                    ("config5 decode-only sample: Llama-3-8B shape random init, bf16, TP by KV "
+                     "head; the running contexts U[8192,32768] at 95% pool occupancy (shuffled "
+                     "free list), no waiting queue: every step decodes them all"),
         "device_status": eng.kv.pool.status(),
     }
     if clocks is not None:
@@ -1012,13 +1131,16 @@ def engine5_arm(args):
     """`--workload engine5`: the config-5 engine alone (see run_engine5), one JSON line."""
     import torch.distributed as dist
     world, rank, dev = _dist_setup()
-    res = run_engine5(args, world, rank, dev, args.steps, args.warmup, sample_clocks=True)
+    res = run_engine5(args, world, rank, dev, args.steps, args.warmup, sample_clocks=True,
+                      queue=not args.decode_only)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return 0
     line = {
-        "metric": "engine output tokens/s (config 5, long context under preemption)",
+        "metric": ("engine output tokens/s (config 5, long context under preemption)"
+                   if not args.decode_only else
+                   "engine output tokens/s (config 5, decode-only sample)"),
         "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
@@ -1315,15 +1437,19 @@ def main():
     ap.add_argument("--rate", type=float, default=20.0,
                     help="engine4: arrivals per second (<= 0: all requests at t=0)")
     ap.add_argument("--seconds", type=float, default=120.0,
-                    help="engine4 --impl reference: time box of the reference engine's run")
+                    help="engine4/engine5 --impl reference: time box of the reference engine's "
+                         "run")
     ap.add_argument("--kv-gb", type=float, default=40.0, help="engine: KV pool GB per GPU")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="engine5: leave out the waiting queue (the sample the reference's engine "
+                         "runs with --impl reference)")
     args = ap.parse_args()
     if args.workload == "config3":
         return config3_arm(args)
     if args.workload == "engine4":
         return reference_engine4_arm(args) if args.impl == "reference" else engine4_arm(args)
     if args.workload == "engine5":
-        return engine5_arm(args)
+        return reference_engine5_arm(args) if args.impl == "reference" else engine5_arm(args)
     if args.workload == "swap":
         return swap_arm(args)
     if args.workload == "meta":
