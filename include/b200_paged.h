@@ -145,8 +145,8 @@ int b200_paged_decode(const B200DecodeParams* p, void* workspace, size_t workspa
 int b200_paged_decode_static(const B200DecodeParams* p, void* stream);
 
 /* Split size of the decode plan, in tokens (rounded up to a multiple of 16); 0 restores the
- * built-in rule: 4096 tokens, halved (down to 64) while the batch would give fewer than 16
- * (sequence, split, KV head) work items per SM, i.e. 8 per resident CTA. */
+ * built-in rule: 2048 tokens, halved (down to 512) while the batch would give fewer
+ * (sequence, split, KV head) work items than half the SMs. */
 void b200_set_decode_split_tokens(int32_t tokens);
 
 /* ============================================================================================

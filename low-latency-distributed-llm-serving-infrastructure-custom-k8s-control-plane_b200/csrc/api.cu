@@ -180,17 +180,21 @@ DecodePlan make_decode_plan(const B200DecodeParams& p) {
   pl.hpc = G < 8 ? G : 8;
   pl.items_per_split = p.geom.num_kv_heads * pl.nchunks;
   const int64_t max_ctx = p.max_context_len > 0 ? p.max_context_len : 1;
-  // Split size: as long as possible (each split writes and re-reads a partial and adds a merge),
-  // but short enough that there are at least 8 (sequence, split, head) items per resident CTA
-  // (2 per SM) for the work stealing to balance the tail.  Measured on config 2 (256 sequences,
-  // lognormal contexts <= 4096): split 256 / 512 / 1024 / 2048 / 4096 reach 61 / 78 / 88 / 91 /
-  // 89 % of the HBM copy peak; this rule picks 2048 there.
+  // Split size: 2048 tokens.  Each split writes and re-reads a partial and adds a merge, so
+  // shorter splits only pay when a batch would otherwise leave most SMs without work: the split
+  // halves (not below 512) while there are fewer (sequence, split, head) items than half the SMs.
+  // Measured GB/s (bf16, GQA 4, D 128) for splits 512 / 1024 / 2048 / 4096: config 2 (256
+  // sequences, lognormal <= 4096) 4666 / 5300 / 5549 / 5270; config 5 at TP 1 (14 sequences,
+  // 8k-32k) 4476 / 4900 / 5207 / 5196; at TP 8 (115 sequences, one KV head) 4438 / 5063 / 5193 /
+  // 5224; 64 sequences of ~600 tokens 2949 / 3195 / 3254 / 3250; 32 sequences <= 4096 2869 /
+  // 2968 / 2872 / 2142; one 32k sequence 1702 / 2299 / 2479 / 1842.  (The earlier rule, at least
+  // 16 items per SM, picked 1024 down to 64 on all but config 2: 339 GB/s for the 32k sequence.)
   int split = g_split_override.load(std::memory_order_relaxed);
   if (split <= 0) {
-    split = 4096;
-    while (split > 64 &&
+    split = 2048;
+    while (split > 512 &&
            static_cast<int64_t>(p.num_seqs) * ((max_ctx + split - 1) / split) * pl.items_per_split <
-               16LL * num_sms())
+               num_sms() / 2)
       split /= 2;
   }
   pl.split_tokens = split;

@@ -53,8 +53,8 @@ def _decode_workspace_layout(S, max_ctx, split, hkv=8, G=4, D=128):
 
 def test_decode_split_rule_on_host(pkg):
     """Pins the split rule through the workspace size (host arithmetic, no GPU needed; without a
-    device the library plans for 148 SMs): the longest power-of-two split from 4096 down to 64
-    that leaves at least 8 (sequence, split, kv head) items per resident CTA (2 per SM)."""
+    device the library plans for 148 SMs): 2048-token splits, halved down to 512 while there are
+    fewer (sequence, split, kv head) items than half the SMs."""
     from llm_serving_b200 import _native as N
     L = N.lib()
 
@@ -68,7 +68,10 @@ def test_decode_split_rule_on_host(pkg):
     # config 2: 256 sequences, contexts up to 4096 -> 2048-token splits
     assert ws(256, 4096) == _decode_workspace_layout(256, 4096, 2048)
     assert ws(256, 4096) != _decode_workspace_layout(256, 4096, 4096)
-    # a long-context batch of 14 sequences -> 1024
-    assert ws(14, 33792) == _decode_workspace_layout(14, 33792, 1024)
-    # a tiny batch bottoms out at 64
-    assert ws(4, 700) == _decode_workspace_layout(4, 700, 64)
+    # a long-context batch of 14 sequences, and a single 32k sequence (128 items) -> 2048
+    assert ws(14, 33792) == _decode_workspace_layout(14, 33792, 2048)
+    assert ws(1, 32768) == _decode_workspace_layout(1, 32768, 2048)
+    # two sequences of 4096 give 32 items at 2048 -> 1024 (64 items) -> 512 (128 items)
+    assert ws(2, 4096) == _decode_workspace_layout(2, 4096, 512)
+    # a tiny batch bottoms out at 512
+    assert ws(4, 700) == _decode_workspace_layout(4, 700, 512)
