@@ -460,6 +460,7 @@ def ours_arm(args):
             N.lib().b200_set_prefill_kernel(args.prefill_kernel)
         prefill = prefill_measure(dev, 20, 3)
         prefill["kernel_selector"] = args.prefill_kernel
+        prefill["long_prompts"] = prefill_long_measure(dev)
     peak, peak_kind = load_peaks()
     ms_per_step = elapsed_ms / args.steps
     value = world * total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -1151,19 +1152,10 @@ def engine5_arm(args):
     return 0
 
 
-def prefill_measure(dev, steps, warmup):
-    """K3 alone on the 16 prefill chunks of the config-3 step (lengths U[128,2048] on prior
-    contexts U[0,2048], GQA 32/8, D 128, bf16): CUDA-event time of the paged_prefill call and
-    its causal QK^T + PV flops against the measured dense bf16 peak."""
+def _prefill_time_ms(dev, pre, steps, warmup):
+    """CUDA-event time of one paged_prefill call over the workload `pre` (bf16, random K/V)."""
     import torch
-    import __graft_entry__
-    pkg = __graft_entry__.load_package()
     from llm_serving_b200 import paged_ops
-    full = pkg.workloads.config3(seed=0)
-    npre = 16
-    pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
-                               new_token_counts=full.new_token_counts[:npre], num_query_heads=32,
-                               num_kv_heads=8, head_dim=128, block_size=16)
     g = torch.Generator(device=dev)
     g.manual_seed(5)
     shape = (1, pre.total_blocks, pre.block_size, pre.num_kv_heads, pre.head_dim)
@@ -1190,14 +1182,35 @@ def prefill_measure(dev, steps, warmup):
         call()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / steps
-    flops = attention_flops(pre)
-    peak, src = 1590.0, "fallback"
+    return e0.elapsed_time(e1) / steps
+
+
+def _bf16_peaks():
+    peak, sustained, src = 1590.0, None, "fallback"
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peak, src = float(json.load(f)["bf16_tflops"]), "measured"
+            mp = json.load(f)
+        peak, src = float(mp["bf16_tflops"]), "measured"
+        sustained = float(mp["bf16_tflops_sustained"]) if "bf16_tflops_sustained" in mp else None
     except Exception:
         pass
+    return peak, sustained, src
+
+
+def prefill_measure(dev, steps, warmup):
+    """K3 alone on the 16 prefill chunks of the config-3 step (lengths U[128,2048] on prior
+    contexts U[0,2048], GQA 32/8, D 128, bf16): CUDA-event time of the paged_prefill call and
+    its causal QK^T + PV flops against the measured dense bf16 peak."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    full = pkg.workloads.config3(seed=0)
+    npre = 16
+    pre = pkg.workloads.custom(seed=1, context_lens=full.context_lens[:npre],
+                               new_token_counts=full.new_token_counts[:npre], num_query_heads=32,
+                               num_kv_heads=8, head_dim=128, block_size=16)
+    ms = _prefill_time_ms(dev, pre, steps, warmup)
+    flops = attention_flops(pre)
+    peak, _, src = _bf16_peaks()
     tflops = flops / (ms * 1e-3) / 1e12
     return {"kernel": "b200_paged_prefill (prefill_tc_kernel, tcgen05)",
             "workload": "the 16 prefill chunks of the config-3 step (%d new tokens)"
@@ -1206,6 +1219,32 @@ def prefill_measure(dev, steps, warmup):
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
                          "peak_source": src + " (burst bf16 GEMM)"}}
+
+
+def prefill_long_measure(dev, steps=5, warmup=3):
+    """K3 on the prompts config 5 recomputes after a preemption: single causal prefills of 8192,
+    16384 and 32768 tokens (no cached prefix; GQA 32/8, D 128, bf16), each timed alone.  Long
+    prompts make long work items, so the item changes that bound the config-3 chunks weigh
+    little here.  The 32k launch runs ~8 ms back to back, so the sustained GEMM figure under
+    the power cap is its fairer denominator; both fractions are given."""
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    peak, sustained, src = _bf16_peaks()
+    rows = []
+    for n in (8192, 16384, 32768):
+        pre = pkg.workloads.custom(seed=1, context_lens=np.array([n]),
+                                   new_token_counts=np.array([n]), num_query_heads=32,
+                                   num_kv_heads=8, head_dim=128, block_size=16)
+        ms = _prefill_time_ms(dev, pre, steps, warmup)
+        tf = attention_flops(pre) / (ms * 1e-3) / 1e12
+        row = {"tokens": n, "ms": round(ms, 4), "tflops": round(tf, 1),
+               "frac_of_burst_peak": round(tf / peak, 4)}
+        if sustained:
+            row["frac_of_sustained_peak"] = round(tf / sustained, 4)
+        rows.append(row)
+    return {"workload": "config-5 recompute prompts: single causal prefills (no prefix)",
+            "peak_source": src, "burst_peak": peak, "sustained_peak": sustained,
+            "prompts": rows}
 
 
 def swap_arm(args):
