@@ -1,6 +1,6 @@
-// K3, the default tensor-core prefill (b200_set_prefill_two_tiles(0) selects the one-tile kernel
-// of prefill.cu instead): two 128-row query tiles per work item, one per softmax warpgroup, against
-// one stream of 128-key K/V tiles.
+// K3, the default tensor-core prefill (b200_set_prefill_kernel(0) selects the one-tile kernel of
+// prefill.cu instead, 2 the two-stream kernel of prefill_ds.cu): two 128-row query tiles per work
+// item, one per softmax warpgroup, against one stream of 128-key K/V tiles.
 //
 // One work item = (sequence, pair of query tiles of TQ = 128/G tokens each, KV head).  Softmax
 // warpgroup w owns query tile w (rows g*TQ + t of tokens [t_begin + w*TQ, t_begin + (w+1)*TQ)) for
@@ -23,10 +23,11 @@
 // SFull wait, and it cannot arrive OEmpty again before the MMA warp consumed the previous arrival
 // (that needs PV_w of this item); a warpgroup without rows in the item (the last pair of a sequence
 // may hold one tile) waits Begin_w instead, which the MMA warp arrives after that OEmpty_w wait.
-// So every parity wait is unambiguous.  V rows past the item's last key in its last tile are zeroed (masked P is exactly 0,
-// but 0 * NaN from an unwritten slot is not) by warpgroup 0 when it attends that tile (its softmax
-// runs first), else by warpgroup 1; the MMA warp waits for that warpgroup's P before issuing
-// either PV on the tile.
+// So every parity wait is unambiguous.
+// V rows past the item's last key in its last tile are zeroed (masked P is exactly 0, but 0 * NaN
+// from an unwritten slot is not) by warpgroup 0 when it attends that tile (its softmax runs
+// first), else by warpgroup 1; the MMA warp waits for that warpgroup's P before issuing either PV
+// on the tile.
 // Epilogue: each softmax warp stages its 32 output rows, 64 columns at a time, in its own 4 KB of
 // shared memory (16-byte chunks XOR-swizzled by row), and writes them back as whole 128-byte row
 // segments, four rows per store instruction.
