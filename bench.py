@@ -458,7 +458,8 @@ def ours_arm(args):
     if world == 1 and not args.no_prefill:
         if args.prefill_kernel is not None:
             N.lib().b200_set_prefill_kernel(args.prefill_kernel)
-        prefill = prefill_measure(dev, 20, 3)
+        prefill = prefill_measure(dev, 20, 3,
+                                  1 if args.prefill_kernel is None else args.prefill_kernel)
         prefill["kernel_selector"] = args.prefill_kernel
         prefill["long_prompts"] = prefill_long_measure(dev)
     peak, peak_kind = load_peaks()
@@ -1197,7 +1198,10 @@ def _bf16_peaks():
     return peak, sustained, src
 
 
-def prefill_measure(dev, steps, warmup):
+PREFILL_KERNEL_NAMES = {0: "prefill_tc_kernel", 1: "prefill_q2_kernel", 2: "prefill_ds_kernel"}
+
+
+def prefill_measure(dev, steps, warmup, selector=1):
     """K3 alone on the 16 prefill chunks of the config-3 step (lengths U[128,2048] on prior
     contexts U[0,2048], GQA 32/8, D 128, bf16): CUDA-event time of the paged_prefill call and
     its causal QK^T + PV flops against the measured dense bf16 peak."""
@@ -1212,7 +1216,7 @@ def prefill_measure(dev, steps, warmup):
     flops = attention_flops(pre)
     peak, _, src = _bf16_peaks()
     tflops = flops / (ms * 1e-3) / 1e12
-    return {"kernel": "b200_paged_prefill (prefill_tc_kernel, tcgen05)",
+    return {"kernel": "b200_paged_prefill (%s, tcgen05)" % PREFILL_KERNEL_NAMES[selector],
             "workload": "the 16 prefill chunks of the config-3 step (%d new tokens)"
                         % pre.num_tokens,
             "ms": round(ms, 4), "flops": flops, "tflops": round(tflops, 2),
