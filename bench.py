@@ -56,9 +56,9 @@ def load_peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def load_traffic():
-    """DRAM bytes per decode launch from the committed ncu summary (or None)."""
-    path = os.path.join(ROOT, "profiles", "paged_decode_config2.md")
+def load_traffic(profile="paged_decode_config2.md"):
+    """DRAM bytes per launch of a profiled kernel, from its committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", profile)
     try:
         with open(path) as f:
             for line in f:
@@ -1448,6 +1448,173 @@ def meta_arm(args):
     return 0
 
 
+def config1_inputs_np(seed=0, value_seed=1):
+    """Config 1 as the reference's binding receives it: 8 decode sequences (contexts U[1,512]),
+    12/12 heads, D 64, BS 16, fp32 N(0,1) values in a 512-block pool; the gather slots are each
+    sequence's context slots in order and the (1, 1, 8, Nctx) mask lets query s see only its own
+    sequence's slots -- what PagedStepContext builds for a decode step
+    (app/model/paged_attention.py:64-69, :92-118).  Same recipe (and seeds) as the config-1
+    golden fixture."""
+    import __graft_entry__
+    b = __graft_entry__.load_package().workloads.config1(seed)
+    rng = np.random.default_rng(value_seed)
+    shape = (1, b.total_blocks, b.block_size, b.num_kv_heads, b.head_dim)
+    kc = rng.standard_normal(shape, dtype=np.float32)
+    vc = rng.standard_normal(shape, dtype=np.float32)
+    q = rng.standard_normal((1, b.num_query_heads, b.num_seqs, b.head_dim), dtype=np.float32)
+    ctx = b.context_lens
+    gs = np.concatenate([np.asarray(t, np.int64)[np.arange(c) // b.block_size] * b.block_size +
+                         np.arange(c) % b.block_size
+                         for t, c in zip(b.tables, ctx)]).astype(np.int32)
+    owner = np.repeat(np.arange(b.num_seqs), ctx)
+    mask = (owner[None, :] == np.arange(b.num_seqs)[:, None]).astype(np.uint8)[None, None]
+    return b, q, kc, vc, gs, mask
+
+
+def config1_arm(args):
+    """Config 1 through the reference-signature C symbol ``paged_attention``
+    (csrc/include/paged_kernels.h:22-34; the fp32 masked row kernel behind it), one call for the
+    whole decode batch with the dense decode mask, the way NativePagedBackend.attend drives the
+    binding (app/model/attention_backends.py:108-117).  value = useful bytes of the step (each
+    sequence's K and V rows once, plus Q and O) / CUDA-event time of the call on device-resident
+    inputs.  The whole cache (50 MB) fits in L2, so a 256 MB buffer is written between timed
+    calls, outside the timed events.  e2e adds to every step the copy of Q, the gather slots and
+    the mask from one pinned host buffer (one copy) and the read-back of the output (the cache
+    stays resident, as it does in a server).  --impl reference (and the cpu_baseline leg): the reference's own
+    kernel built from its sources (oracle/_ref), else the C port, on all host cores, on the same
+    inputs; its output is compared with the GPU's (fp32: 1e-5 relative)."""
+    import ctypes
+    import torch
+    b, q, kc, vc, gs, mask = config1_inputs_np()
+    nq, hq, d = b.num_seqs, b.num_query_heads, b.head_dim
+    useful = int(b.context_lens.sum()) * b.num_kv_heads * d * 4 * 2 + 2 * q.size * 4
+    workload = ("config1: the paged_attention C symbol (fp32 masked form), 8 decode sequences, "
+                "ctx U[1,512], 12/12 heads, D 64, BS 16, 512-block pool, one call per step")
+
+    def cpu_leg(min_seconds):
+        from oracle import oracle as O
+        cores = os.cpu_count() or 1
+        if O.RefKernel.available():
+            k = O.RefKernel()
+            k.set_threads(cores)
+            call, kind = k.paged_attention, "reference"
+        else:
+            os.environ["OMP_NUM_THREADS"] = str(cores)
+            call, kind = O.paged_attention, "port"
+        out = call(q, kc, vc, 0, gs, mask, b.scale)
+        t0 = time.perf_counter()
+        n = 0
+        while n < 3 or time.perf_counter() - t0 < min_seconds:
+            call(q, kc, vc, 0, gs, mask, b.scale)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return useful / dt / 1e9, dt, kind, cores, n, np.asarray(out).reshape(1, nq, hq, d)
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        gbs, dt, kind, cores, n, _ = cpu_leg(max(2.0, args.cpu_seconds / 5))
+        sample = f"the whole config-1 step, {n} calls ({dt * 1e3:.3f} ms each)"
+        print(json.dumps({
+            "impl": "reference", "metric": "paged_attention (config 1) GB/s", "value": round(gbs, 4),
+            "unit": "GB/s", "n_gpus": 1, "steps": n, "warmup": 1, "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic", "ms_per_step": round(dt * 1e3, 4),
+            "config": {"workload": workload},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}))
+        return 0
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from llm_serving_b200 import _native as N
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    tk, tv = torch.from_numpy(kc).to(dev), torch.from_numpy(vc).to(dev)
+    tq, tgs, tm = (torch.from_numpy(x).to(dev) for x in (q, gs, mask))
+    out = torch.empty((1, nq, hq, d), dtype=torch.float32, device=dev)
+    dims = N.PagedAttentionDims(hq, nq, d, kc.shape[0], kc.shape[1], kc.shape[2], kc.shape[3],
+                                gs.shape[0])
+    fn = N.lib().paged_attention
+    stream = torch.cuda.current_stream(dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    scale = ctypes.c_float(b.scale)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def call(qp, gp, mp, op):
+        fn(qp, tk.data_ptr(), tv.data_ptr(), 0, dims, gp, mp, scale, op, None, sptr)
+
+    for _ in range(max(args.warmup, 3)):
+        call(tq.data_ptr(), tgs.data_ptr(), tm.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record(stream)
+        call(tq.data_ptr(), tgs.data_ptr(), tm.data_ptr(), out.data_ptr())
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
+    dev_out = out.cpu().numpy()
+    # e2e: per step, Q, gather slots and mask in from one pinned host buffer (one copy; each
+    # array at a 256-byte aligned offset), the output back out
+    offs, total = [], 0
+    for x in (q, gs, mask):
+        offs.append(total)
+        total += -(-x.nbytes // 256) * 256
+    pin = torch.empty(total, dtype=torch.uint8).pin_memory()
+    for x, o in zip((q, gs, mask), offs):
+        pin[o:o + x.nbytes].copy_(torch.from_numpy(np.ascontiguousarray(x).view(np.uint8).ravel()))
+    dbuf = torch.empty(total, dtype=torch.uint8, device=dev)
+    dq, dgs, dm = (dbuf.data_ptr() + o for o in offs)
+    hout = torch.empty((1, nq, hq, d), dtype=torch.float32).pin_memory()
+    h2d = total
+    d2h = hout.numel() * 4
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for e0, e1 in ev2:
+        flush.zero_()
+        e0.record(stream)
+        dbuf.copy_(pin, non_blocking=True)
+        call(dq, dgs, dm, out.data_ptr())
+        hout.copy_(out, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_e2e = sum(e0.elapsed_time(e1) for e0, e1 in ev2) / args.steps
+    peak, peak_kind = load_peaks()
+    gbs = useful / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "paged_attention (config 1) GB/s", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload, "l2": "256 MB buffer written between timed calls",
+                   "useful_bytes_per_step": useful},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 3), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 5),
+                     "traffic": load_traffic("paged_attention_masked_config1.md"),
+                     "peak_source": peak_kind,
+                     "kernel": "mask_attn_kernel: 96 CTAs (8 query rows x 12 heads), "
+                               "latency-bound"},
+        "e2e": {"value": round(useful / (ms_e2e * 1e-3) / 1e9, 3), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(ms_e2e, 5),
+                "output_matches_device_run": bool(np.array_equal(hout.numpy(), dev_out))},
+        "gpu_launches": args.steps,
+    }
+    if not args.no_cpu:
+        cgbs, dt, kind, cores, n, ref = cpu_leg(max(2.0, args.cpu_seconds / 5))
+        line["cpu_baseline"] = {"value": round(cgbs, 4), "unit": "GB/s", "cores": cores,
+                                "kind": kind,
+                                "sample": f"the whole config-1 step, {n} calls "
+                                          f"({dt * 1e3:.3f} ms each)"}
+        line["max_rel_vs_cpu"] = float(np.abs(dev_out - ref).max() / np.abs(ref).max())
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1473,8 +1640,8 @@ def main():
                     help="tensor-core prefill kernel (config3 and the prefill leg): 0 one query "
                          "tile per item, 1 two tiles per item, 2 two streams per CTA; default: "
                          "the library's")
-    ap.add_argument("--workload", choices=["config2", "config3", "engine4", "engine5", "swap",
-                                           "meta"],
+    ap.add_argument("--workload", choices=["config1", "config2", "config3", "engine4", "engine5",
+                                           "swap", "meta"],
                     default="config2")
     ap.add_argument("--requests", type=int, default=200, help="engine4: requests to run")
     ap.add_argument("--rate", type=float, default=20.0,
@@ -1487,6 +1654,8 @@ def main():
                     help="engine5: leave out the waiting queue (the sample the reference's engine "
                          "runs with --impl reference)")
     args = ap.parse_args()
+    if args.workload == "config1":
+        return config1_arm(args)
     if args.workload == "config3":
         return config3_arm(args)
     if args.workload == "engine4":

@@ -76,3 +76,31 @@ def test_roofline_arithmetic_matches_the_quoted_figures(pkg):
                                num_kv_heads=8, head_dim=128, block_size=16)
     assert pre.num_tokens == 17543
     assert bench.attention_flops(pre) == 533616574464
+
+
+def test_config1_bench_inputs_are_the_golden_ones(golden):
+    """The config-1 bench leg feeds the reference-signature symbol the golden fixture's inputs:
+    the same arrays as the fixture generator, and the reference's recorded output from them."""
+    from config1_inputs import config1_inputs
+    b, q, kc, vc, gs, mask = bench.config1_inputs_np()
+    b2, q2, kc2, vc2, gs2, mask2 = config1_inputs()
+    for x, y in ((q, q2), (kc, kc2), (vc, vc2), (gs, gs2), (mask, mask2)):
+        assert x.dtype == y.dtype and np.array_equal(x, y)
+    assert b.scale == b2.scale and mask.shape == (1, 1, b.num_seqs, gs.shape[0])
+
+
+def test_config1_reference_arm_line(capsys):
+    """--workload config1 --impl reference prints one line on the reference contract."""
+    import json
+    import sys
+    argv = sys.argv
+    sys.argv = ["bench.py", "--workload", "config1", "--impl", "reference", "--cpu-seconds", "1"]
+    try:
+        assert bench.main() == 0
+    finally:
+        sys.argv = argv
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "GB/s"
+    assert line["cpu_baseline"]["kind"] in ("reference", "port")
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
