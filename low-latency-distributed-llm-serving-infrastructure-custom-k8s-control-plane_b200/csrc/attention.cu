@@ -13,8 +13,12 @@
 //                          (atomic counter, no spin-waits).
 //  * row_attn_kernel    -- CUDA-core path, one CTA per (query row, kv head, head chunk): fp32
 //                          caches, and shapes outside the tensor-core tile rules.  Block-table
-//                          decode, ragged causal prefill, or the reference's gather-slot + mask
-//                          form (csrc/src/paged_kernels.cpp:7-105 semantics).
+//                          decode or ragged causal prefill.
+//  * mask_attn_kernel   -- the reference's gather-slot + mask form (csrc/src/paged_kernels.cpp:
+//                          7-105 semantics), one CTA of 4-16 warps per (query row, kv head, head
+//                          chunk): the allowed slots of each 2048-slot chunk are compacted in
+//                          shared memory, then attended in groups, the next group's K/V rows
+//                          loading while the current group is computed.
 #include "attention.cuh"
 
 namespace b200 {
@@ -419,31 +423,24 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
   float* l_w = m_w + NW * 8;             // [NW][8]
 
   // Which context does this query row attend?
-  int64_t qrow = row, ctx_begin = 0;
-  int32_t n_ctx = 0, pos = 0, seq = 0;
-  const int32_t* bt_row = nullptr;
-  if (a.mode == kRowMask) {
-    n_ctx = a.num_ctx;
-    pos = 0;
+  int64_t qrow = row;
+  int32_t pos = 0, seq = 0;
+  if (a.cu_q == nullptr) {
+    seq = row;
+    qrow = a.query_rows ? a.query_rows[row] : row;
+    pos = a.ctx_lens[seq] - 1;
   } else {
-    if (a.cu_q == nullptr) {
-      seq = row;
-      qrow = a.query_rows ? a.query_rows[row] : row;
-      pos = a.ctx_lens[seq] - 1;
-    } else {
-      int lo = 0, hi = a.S - 1;  // last s with cu_q[s] <= row
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (a.cu_q[mid] <= row) lo = mid; else hi = mid - 1;
-      }
-      seq = lo;
-      const int32_t count = static_cast<int32_t>(a.cu_q[seq + 1] - a.cu_q[seq]);
-      pos = a.ctx_lens[seq] - count + static_cast<int32_t>(row - a.cu_q[seq]);
+    int lo = 0, hi = a.S - 1;  // last s with cu_q[s] <= row
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.cu_q[mid] <= row) lo = mid; else hi = mid - 1;
     }
-    n_ctx = pos + 1;
-    bt_row = a.bt + static_cast<int64_t>(seq) * a.bt_stride;
+    seq = lo;
+    const int32_t count = static_cast<int32_t>(a.cu_q[seq + 1] - a.cu_q[seq]);
+    pos = a.ctx_lens[seq] - count + static_cast<int32_t>(row - a.cu_q[seq]);
   }
-  (void)ctx_begin;
+  const int32_t n_ctx = pos + 1;
+  const int32_t* bt_row = a.bt + static_cast<int64_t>(seq) * a.bt_stride;
 
   float q[8][NPL];
   float acc[8][NPL];
@@ -458,9 +455,8 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
       acc[g][i] = 0.f;
       q[g][i] = 0.f;
       if (g < nh && d < D) {
-        const T* qp = static_cast<const T*>(a.q) + (a.mode == kRowMask
-                          ? (static_cast<int64_t>(hq0 + g) * a.q_shead + row * a.q_srow)
-                          : (qrow * a.q_srow + static_cast<int64_t>(hq0 + g) * a.q_shead));
+        const T* qp = static_cast<const T*>(a.q) + qrow * a.q_srow +
+                      static_cast<int64_t>(hq0 + g) * a.q_shead;
         q[g][i] = to_f32<T>(qp[d]);
       }
     }
@@ -469,18 +465,12 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
   const int64_t row_elems = static_cast<int64_t>(a.hkv) * D;
   const int64_t layer_base = static_cast<int64_t>(a.layer) * a.nb * a.bs * row_elems;
   for (int cpos = warp; cpos < n_ctx; cpos += NW) {
-    int64_t slot;
-    if (a.mode == kRowMask) {
-      if (!a.mask[row * static_cast<int64_t>(a.num_ctx) + cpos]) continue;
-      slot = a.gather[cpos];
-    } else {
-      const int32_t blk = bt_row[cpos / a.bs];
-      if (blk < 0 || blk >= a.nb) {
-        if (lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
-        continue;
-      }
-      slot = static_cast<int64_t>(blk) * a.bs + cpos % a.bs;
+    const int32_t blk = bt_row[cpos / a.bs];
+    if (blk < 0 || blk >= a.nb) {
+      if (lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+      continue;
     }
+    const int64_t slot = static_cast<int64_t>(blk) * a.bs + cpos % a.bs;
     if (slot < 0 || slot >= static_cast<int64_t>(a.nb) * a.bs) {
       if (lane == 0) flag_status(a.status, B200_DEVICE_BAD_SLOT);
       continue;
@@ -550,6 +540,206 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
 }
 
 // ============================================================================================
+// Gather-slot + mask form (the reference's paged_attention signature)
+// ============================================================================================
+
+constexpr int kMaskChunk = 2048;  // context positions compacted per pass
+
+// One CTA of NW warps per (query row, kv head, head chunk).  Each pass compacts the positions of
+// kMaskChunk context slots that the row's mask allows into a shared-memory list of gather slots
+// (per-thread counts, block-wide prefix sum), so a masked-out position costs one byte load here
+// only.  The warps then take groups of U list entries: a group's K/V rows are loaded together
+// and its U dot products reduced together, and the next group's rows are loaded before the
+// current group is computed, so each warp keeps two groups of loads in flight.  Per group and
+// head the running max moves once: one rescale, then the U exponentials against the new max.
+// NW is 16 for D <= 64, 8 for D = 128 and 4 for D = 256 (the merge buffers stay at 32 KB).
+template <typename T, int NPL, int U, int NW>
+__global__ void __launch_bounds__(NW * 32) mask_attn_kernel(RowArgs a) {
+  constexpr int kThreads = NW * 32;
+  constexpr int kPer = kMaskChunk / kThreads;
+  static_assert(kPer * kThreads == kMaskChunk && kPer <= 32, "compaction split");
+  extern __shared__ float rsm[];
+  __shared__ int32_t list[kMaskChunk];
+  __shared__ int32_t warp_tot[NW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x;
+  const int h = blockIdx.y / a.nchunks;
+  const int cch = blockIdx.y - h * a.nchunks;
+  const int nh = min(8, a.group - cch * 8);
+  const int hq0 = h * a.group + cch * 8;
+  const int D = a.head_dim;
+  float* o_w = rsm;                      // [NW][8][D]
+  float* m_w = o_w + NW * 8 * D;         // [NW][8]
+  float* l_w = m_w + NW * 8;             // [NW][8]
+
+  float q[8][NPL], acc[8][NPL], m[8], l[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      const int d = lane + 32 * i;
+      acc[g][i] = 0.f;
+      q[g][i] = 0.f;
+      if (g < nh && d < D)
+        q[g][i] = to_f32<T>(static_cast<const T*>(a.q)[static_cast<int64_t>(hq0 + g) * a.q_shead +
+                                                       row * a.q_srow + d]);
+    }
+  }
+
+  const int64_t row_elems = static_cast<int64_t>(a.hkv) * D;
+  const int64_t layer_base = static_cast<int64_t>(a.layer) * a.nb * a.bs * row_elems;
+  const int64_t n_slots = static_cast<int64_t>(a.nb) * a.bs;
+  const uint8_t* mrow = a.mask + static_cast<int64_t>(row) * a.num_ctx;
+
+  // K/V rows of list entries [e0, e0 + U) (entries at or past `total`, and slots outside the
+  // cache, are skipped; the latter set a status bit)
+  auto load_group = [&](int e0, int total, float (&kv)[U][NPL], float (&vv)[U][NPL],
+                        bool (&ok)[U]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u;
+      const int64_t slot = e < total ? static_cast<int64_t>(list[e]) : 0;
+      ok[u] = e < total && slot >= 0 && slot < n_slots;
+      if (e < total && !ok[u] && lane == 0) flag_status(a.status, B200_DEVICE_BAD_SLOT);
+      const int64_t base = layer_base + (ok[u] ? slot : 0) * row_elems + h * D;
+      const T* kp = static_cast<const T*>(a.kc) + base;
+      const T* vp = static_cast<const T*>(a.vc) + base;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        const int d = lane + 32 * i;
+        kv[u][i] = ok[u] && d < D ? to_f32<T>(kp[d]) : 0.f;
+        vv[u][i] = ok[u] && d < D ? to_f32<T>(vp[d]) : 0.f;
+      }
+    }
+  };
+
+  for (int c0 = 0; c0 < a.num_ctx; c0 += kMaskChunk) {
+    // ---- compaction: this thread's kPer positions, then its offset in the pass's list
+    const int p0 = c0 + tid * kPer;
+    uint32_t bits = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (p0 + i < a.num_ctx && mrow[p0 + i]) bits |= 1u << i;
+    const int cnt = __popc(bits);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int off = incl - cnt, total = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const int t = warp_tot[w];
+      if (w < warp) off += t;
+      total += t;
+    }
+    while (bits) {
+      const int i = __ffs(bits) - 1;
+      bits &= bits - 1;
+      list[off++] = a.gather[p0 + i];
+    }
+    __syncthreads();
+
+    // ---- attention over the pass's allowed slots: group e0 computed while group e0 + NW*U loads
+    float kv[U][NPL], vv[U][NPL];
+    bool ok[U];
+    load_group(warp * U, total, kv, vv, ok);
+    for (int e0 = warp * U; e0 < total; e0 += NW * U) {
+      float kv2[U][NPL], vv2[U][NPL];
+      bool ok2[U];
+      load_group(e0 + NW * U, total, kv2, vv2, ok2);
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        if (g >= nh) break;
+        float sv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          float part = 0.f;
+#pragma unroll
+          for (int i = 0; i < NPL; ++i) part = fmaf(q[g][i], kv[u][i], part);
+          sv[u] = part;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int u = 0; u < U; ++u) sv[u] += __shfl_xor_sync(0xffffffffu, sv[u], o);
+        float mx = m[g];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          sv[u] *= a.scale;
+          if (ok[u]) mx = fmaxf(mx, sv[u]);
+        }
+        if (mx == -INFINITY) continue;  // no allowed slot in the group yet
+        const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mx);
+        l[g] *= alpha;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[g][i] *= alpha;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (!ok[u]) continue;
+          const float pw = expf(sv[u] - mx);
+          l[g] += pw;
+#pragma unroll
+          for (int i = 0; i < NPL; ++i) acc[g][i] = fmaf(pw, vv[u][i], acc[g][i]);
+        }
+        m[g] = mx;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        ok[u] = ok2[u];
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+          kv[u][i] = kv2[u][i];
+          vv[u][i] = vv2[u][i];
+        }
+      }
+    }
+    __syncthreads();  // the next pass rewrites the list and the warp totals
+  }
+
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      m_w[warp * 8 + g] = m[g];
+      l_w[warp * 8 + g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) o_w[(warp * 8 + g) * D + d] = acc[g][i];
+    }
+  __syncthreads();
+  for (int idx = tid; idx < nh * D; idx += kThreads) {
+    const int g = idx / D, d = idx - g * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, m_w[w * 8 + g]);
+    float o = 0.f, L = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float mw = m_w[w * 8 + g];
+        if (mw == -INFINITY) continue;
+        const float wt = expf(mw - M);
+        o += wt * o_w[(w * 8 + g) * D + d];
+        L += wt * l_w[w * 8 + g];
+      }
+    }
+    T* op = static_cast<T*>(a.out) + static_cast<int64_t>(row) * a.o_srow +
+            static_cast<int64_t>(hq0 + g) * a.o_shead;
+    op[d] = from_f32<T>(L > 0.f ? o / L : 0.f);
+  }
+}
+
+// ============================================================================================
 // Launchers
 // ============================================================================================
 
@@ -607,6 +797,16 @@ static cudaError_t launch_row_t(const RowArgs& a, int rows, cudaStream_t stream)
   const dim3 grid(rows, a.hkv * a.nchunks);
   const int smem = (4 * 8 * a.head_dim + 2 * 4 * 8) * 4;
   const int npl = (a.head_dim + 31) / 32;
+  if (a.mode == kRowMask) {
+    // NW warps: 16 / 16 / 8 / 4; merge buffers (NW * 8 * D + 2 * NW * 8) floats, <= 33.8 KB
+    auto mask_smem = [&](int nw) { return (nw * 8 * a.head_dim + 2 * nw * 8) * 4; };
+    if (npl <= 1) mask_attn_kernel<T, 1, 4, 16><<<grid, 512, mask_smem(16), stream>>>(a);
+    else if (npl <= 2) mask_attn_kernel<T, 2, 4, 16><<<grid, 512, mask_smem(16), stream>>>(a);
+    else if (npl <= 4) mask_attn_kernel<T, 4, 2, 8><<<grid, 256, mask_smem(8), stream>>>(a);
+    else if (npl <= 8) mask_attn_kernel<T, 8, 1, 4><<<grid, 128, mask_smem(4), stream>>>(a);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+  }
   if (npl <= 1) row_attn_kernel<T, 1><<<grid, 128, smem, stream>>>(a);
   else if (npl <= 2) row_attn_kernel<T, 2><<<grid, 128, smem, stream>>>(a);
   else if (npl <= 4) row_attn_kernel<T, 4><<<grid, 128, smem, stream>>>(a);
