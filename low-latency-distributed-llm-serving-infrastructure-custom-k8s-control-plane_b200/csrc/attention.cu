@@ -616,12 +616,17 @@ __global__ void __launch_bounds__(NW * 32) mask_attn_kernel(RowArgs a) {
   };
 
   for (int c0 = 0; c0 < a.num_ctx; c0 += kMaskChunk) {
-    // ---- compaction: this thread's kPer positions, then its offset in the pass's list
+    // ---- compaction: this thread's kPer positions (their gather slots load together with the
+    // mask bytes), then its offset in the pass's list
     const int p0 = c0 + tid * kPer;
     uint32_t bits = 0;
+    int32_t gv[kPer];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i)
-      if (p0 + i < a.num_ctx && mrow[p0 + i]) bits |= 1u << i;
+    for (int i = 0; i < kPer; ++i) {
+      const bool in = p0 + i < a.num_ctx;
+      gv[i] = in ? a.gather[p0 + i] : 0;
+      if (in && mrow[p0 + i]) bits |= 1u << i;
+    }
     const int cnt = __popc(bits);
     int incl = cnt;
 #pragma unroll
@@ -638,11 +643,9 @@ __global__ void __launch_bounds__(NW * 32) mask_attn_kernel(RowArgs a) {
       if (w < warp) off += t;
       total += t;
     }
-    while (bits) {
-      const int i = __ffs(bits) - 1;
-      bits &= bits - 1;
-      list[off++] = a.gather[p0 + i];
-    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if ((bits >> i) & 1u) list[off++] = gv[i];
     __syncthreads();
 
     // ---- attention over the pass's allowed slots: group e0 computed while group e0 + NW*U loads
