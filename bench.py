@@ -1583,6 +1583,26 @@ def config1_arm(args):
         e1.record(stream)
     torch.cuda.synchronize(dev)
     ms_e2e = sum(e0.elapsed_time(e1) for e0, e1 in ev2) / args.steps
+    # the same batch through the block-table decode API (b200_paged_decode); fp32 caches take the
+    # CUDA-core row kernel
+    from llm_serving_b200 import paged_ops
+    qd = torch.from_numpy(np.ascontiguousarray(q[0].transpose(1, 0, 2))).to(dev)
+    bt = torch.from_numpy(b.block_tables()).to(dev)
+    cl = torch.from_numpy(b.context_lens).to(dev)
+    maxc = int(b.context_lens.max())
+    for _ in range(3):
+        out_bt = paged_ops.paged_decode(qd, tk, tv, 0, bt, cl, b.scale, maxc)
+    torch.cuda.synchronize(dev)
+    ev3 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for e0, e1 in ev3:
+        flush.zero_()
+        e0.record(stream)
+        out_bt = paged_ops.paged_decode(qd, tk, tv, 0, bt, cl, b.scale, maxc)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_bt = sum(e0.elapsed_time(e1) for e0, e1 in ev3) / args.steps
+    bt_out = out_bt.cpu().numpy()[None]
     peak, peak_kind = load_peaks()
     gbs = useful / (ms * 1e-3) / 1e9
     line = {
@@ -1602,7 +1622,12 @@ def config1_arm(args):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(ms_e2e, 5),
                 "output_matches_device_run": bool(np.array_equal(hout.numpy(), dev_out))},
-        "gpu_launches": args.steps,
+        "block_table_decode": {
+            "api": "b200_paged_decode (block tables + context lengths) on the same batch",
+            "kernel": "row_attn_kernel (fp32 caches)", "us": round(ms_bt * 1e3, 2),
+            "gbs": round(useful / (ms_bt * 1e-3) / 1e9, 3),
+            "max_rel_vs_mask_form": float(np.abs(bt_out - dev_out).max() / np.abs(dev_out).max())},
+        "gpu_launches": 3 * args.steps,  # mask form device-resident and e2e, block-table decode
     }
     if not args.no_cpu:
         cgbs, dt, kind, cores, n, ref = cpu_leg(max(2.0, args.cpu_seconds / 5))

@@ -11,9 +11,10 @@
 //                          online softmax, merges its warps in shared memory and, for split
 //                          sequences, the last CTA of a (sequence, kv head) merges the partials
 //                          (atomic counter, no spin-waits).
-//  * row_attn_kernel    -- CUDA-core path, one CTA per (query row, kv head, head chunk): fp32
-//                          caches, and shapes outside the tensor-core tile rules.  Block-table
-//                          decode or ragged causal prefill.
+//  * row_attn_kernel    -- CUDA-core path, one CTA of 4-16 warps per (query row, kv head, head
+//                          chunk): fp32 caches, and shapes outside the tensor-core tile rules.
+//                          Block-table decode or ragged causal prefill; positions in groups, the
+//                          next group's K/V rows loading while the current group is computed.
 //  * mask_attn_kernel   -- the reference's gather-slot + mask form (csrc/src/paged_kernels.cpp:
 //                          7-105 semantics), one CTA of 4-16 warps per (query row, kv head, head
 //                          chunk): the allowed slots of each 2048-slot chunk are compacted in
@@ -407,9 +408,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 // CUDA-core row kernel (fp32 exactness path and shapes outside the tensor-core rules)
 // ============================================================================================
 
-template <typename T, int NPL>
-__global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
-  constexpr int NW = 4;
+// One CTA of NW warps per (query row, kv head, head chunk).  The row's context positions are
+// taken in groups of U consecutive positions per warp: a group's block ids and K/V rows are loaded
+// together, its U dot products reduced together, and the next group's loads are issued before the
+// current group is computed (the same schedule as mask_attn_kernel below).
+template <typename T, int NPL, int U, int NW>
+__global__ void __launch_bounds__(NW * 32) row_attn_kernel(RowArgs a) {
+  constexpr int kThreads = NW * 32;
   extern __shared__ float rsm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x;
@@ -464,42 +469,77 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
 
   const int64_t row_elems = static_cast<int64_t>(a.hkv) * D;
   const int64_t layer_base = static_cast<int64_t>(a.layer) * a.nb * a.bs * row_elems;
-  for (int cpos = warp; cpos < n_ctx; cpos += NW) {
-    const int32_t blk = bt_row[cpos / a.bs];
-    if (blk < 0 || blk >= a.nb) {
-      if (lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
-      continue;
-    }
-    const int64_t slot = static_cast<int64_t>(blk) * a.bs + cpos % a.bs;
-    if (slot < 0 || slot >= static_cast<int64_t>(a.nb) * a.bs) {
-      if (lane == 0) flag_status(a.status, B200_DEVICE_BAD_SLOT);
-      continue;
-    }
-    const T* kp = static_cast<const T*>(a.kc) + layer_base + slot * row_elems + h * D;
-    const T* vp = static_cast<const T*>(a.vc) + layer_base + slot * row_elems + h * D;
-    float kv[NPL], vv[NPL];
+  // K/V rows of positions [c0, c0 + U) (positions at or past n_ctx are skipped; a block id
+  // outside the pool sets a status bit and skips the position)
+  auto load_group = [&](int c0, float (&kv)[U][NPL], float (&vv)[U][NPL], bool (&ok)[U]) {
 #pragma unroll
-    for (int i = 0; i < NPL; ++i) {
-      const int d = lane + 32 * i;
-      kv[i] = d < D ? to_f32<T>(kp[d]) : 0.f;
-      vv[i] = d < D ? to_f32<T>(vp[d]) : 0.f;
+    for (int u = 0; u < U; ++u) {
+      const int cpos = c0 + u;
+      const int32_t blk = cpos < n_ctx ? bt_row[cpos / a.bs] : 0;
+      ok[u] = cpos < n_ctx && blk >= 0 && blk < a.nb;
+      if (cpos < n_ctx && !ok[u] && lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+      const int64_t slot = ok[u] ? static_cast<int64_t>(blk) * a.bs + cpos % a.bs : 0;
+      const T* kp = static_cast<const T*>(a.kc) + layer_base + slot * row_elems + h * D;
+      const T* vp = static_cast<const T*>(a.vc) + layer_base + slot * row_elems + h * D;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        const int d = lane + 32 * i;
+        kv[u][i] = ok[u] && d < D ? to_f32<T>(kp[d]) : 0.f;
+        vv[u][i] = ok[u] && d < D ? to_f32<T>(vp[d]) : 0.f;
+      }
     }
+  };
+  float kv[U][NPL], vv[U][NPL];
+  bool ok[U];
+  load_group(warp * U, kv, vv, ok);
+  for (int c0 = warp * U; c0 < n_ctx; c0 += NW * U) {
+    float kv2[U][NPL], vv2[U][NPL];
+    bool ok2[U];
+    load_group(c0 + NW * U, kv2, vv2, ok2);
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
       if (g >= nh) break;
-      float part = 0.f;
+      float sv[U];
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) part = fmaf(q[g][i], kv[i], part);
+      for (int u = 0; u < U; ++u) {
+        float part = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      const float sv = part * a.scale;
-      const float mn = fmaxf(m[g], sv);
-      const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mn);
-      const float pw = expf(sv - mn);
-      l[g] = l[g] * alpha + pw;
+        for (int i = 0; i < NPL; ++i) part = fmaf(q[g][i], kv[u][i], part);
+        sv[u] = part;
+      }
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) acc[g][i] = fmaf(acc[g][i], alpha, pw * vv[i]);
-      m[g] = mn;
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < U; ++u) sv[u] += __shfl_xor_sync(0xffffffffu, sv[u], o);
+      float mx = m[g];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        sv[u] *= a.scale;
+        if (ok[u]) mx = fmaxf(mx, sv[u]);
+      }
+      if (mx == -INFINITY) continue;  // no valid position in the group yet
+      const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mx);
+      l[g] *= alpha;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) acc[g][i] *= alpha;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!ok[u]) continue;
+        const float pw = expf(sv[u] - mx);
+        l[g] += pw;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[g][i] = fmaf(pw, vv[u][i], acc[g][i]);
+      }
+      m[g] = mx;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      ok[u] = ok2[u];
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        kv[u][i] = kv2[u][i];
+        vv[u][i] = vv2[u][i];
+      }
     }
   }
 
@@ -518,7 +558,7 @@ __global__ void __launch_bounds__(128) row_attn_kernel(RowArgs a) {
       if (d < D) o_w[(warp * 8 + g) * D + d] = acc[g][i];
     }
   __syncthreads();
-  for (int idx = tid; idx < nh * D; idx += 128) {
+  for (int idx = tid; idx < nh * D; idx += kThreads) {
     const int g = idx / D, d = idx - g * D;
     float M = -INFINITY;
 #pragma unroll
@@ -798,11 +838,11 @@ cudaError_t launch_decode_tc(int dtype, int head_dim, const CUtensorMap& km, con
 template <typename T>
 static cudaError_t launch_row_t(const RowArgs& a, int rows, cudaStream_t stream) {
   const dim3 grid(rows, a.hkv * a.nchunks);
-  const int smem = (4 * 8 * a.head_dim + 2 * 4 * 8) * 4;
   const int npl = (a.head_dim + 31) / 32;
+  // NW warps: 16 / 16 / 8 / 4 for NPL 1 / 2 / 4 / 8; merge buffers (NW * 8 * D + 2 * NW * 8)
+  // floats, <= 33.8 KB
+  auto mask_smem = [&](int nw) { return (nw * 8 * a.head_dim + 2 * nw * 8) * 4; };
   if (a.mode == kRowMask) {
-    // NW warps: 16 / 16 / 8 / 4; merge buffers (NW * 8 * D + 2 * NW * 8) floats, <= 33.8 KB
-    auto mask_smem = [&](int nw) { return (nw * 8 * a.head_dim + 2 * nw * 8) * 4; };
     if (npl <= 1) mask_attn_kernel<T, 1, 4, 16><<<grid, 512, mask_smem(16), stream>>>(a);
     else if (npl <= 2) mask_attn_kernel<T, 2, 4, 16><<<grid, 512, mask_smem(16), stream>>>(a);
     else if (npl <= 4) mask_attn_kernel<T, 4, 2, 8><<<grid, 256, mask_smem(8), stream>>>(a);
@@ -810,10 +850,10 @@ static cudaError_t launch_row_t(const RowArgs& a, int rows, cudaStream_t stream)
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
   }
-  if (npl <= 1) row_attn_kernel<T, 1><<<grid, 128, smem, stream>>>(a);
-  else if (npl <= 2) row_attn_kernel<T, 2><<<grid, 128, smem, stream>>>(a);
-  else if (npl <= 4) row_attn_kernel<T, 4><<<grid, 128, smem, stream>>>(a);
-  else if (npl <= 8) row_attn_kernel<T, 8><<<grid, 128, smem, stream>>>(a);
+  if (npl <= 1) row_attn_kernel<T, 1, 4, 16><<<grid, 512, mask_smem(16), stream>>>(a);
+  else if (npl <= 2) row_attn_kernel<T, 2, 4, 16><<<grid, 512, mask_smem(16), stream>>>(a);
+  else if (npl <= 4) row_attn_kernel<T, 4, 2, 8><<<grid, 256, mask_smem(8), stream>>>(a);
+  else if (npl <= 8) row_attn_kernel<T, 8, 1, 4><<<grid, 128, mask_smem(4), stream>>>(a);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
