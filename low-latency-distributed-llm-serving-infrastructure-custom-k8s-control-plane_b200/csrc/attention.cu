@@ -408,6 +408,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 // CUDA-core row kernel (fp32 exactness path and shapes outside the tensor-core rules)
 // ============================================================================================
 
+constexpr int kRowPassBlocks = 256;  // block ids of a row staged in shared memory per pass
+
 // One CTA of NW warps per (query row, kv head, head chunk).  The row's context positions are
 // taken in groups of U consecutive positions per warp: a group's block ids and K/V rows are loaded
 // together, its U dot products reduced together, and the next group's loads are issued before the
@@ -469,15 +471,19 @@ __global__ void __launch_bounds__(NW * 32) row_attn_kernel(RowArgs a) {
 
   const int64_t row_elems = static_cast<int64_t>(a.hkv) * D;
   const int64_t layer_base = static_cast<int64_t>(a.layer) * a.nb * a.bs * row_elems;
-  // K/V rows of positions [c0, c0 + U) (positions at or past n_ctx are skipped; a block id
-  // outside the pool sets a status bit and skips the position)
+  // The row's block ids, kRowPassBlocks per pass, are staged in shared memory first, so a group's
+  // K/V addresses need no global load.  K/V rows of positions [c0, c0 + U) of the pass that starts
+  // at p0 and ends at pend (positions at or past pend are skipped; a block id outside the pool
+  // sets a status bit and skips the position):
+  __shared__ int32_t blk_s[kRowPassBlocks];
+  int p0 = 0, pend = 0;
   auto load_group = [&](int c0, float (&kv)[U][NPL], float (&vv)[U][NPL], bool (&ok)[U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int cpos = c0 + u;
-      const int32_t blk = cpos < n_ctx ? bt_row[cpos / a.bs] : 0;
-      ok[u] = cpos < n_ctx && blk >= 0 && blk < a.nb;
-      if (cpos < n_ctx && !ok[u] && lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
+      const int32_t blk = cpos < pend ? blk_s[(cpos - p0) / a.bs] : 0;
+      ok[u] = cpos < pend && blk >= 0 && blk < a.nb;
+      if (cpos < pend && !ok[u] && lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
       const int64_t slot = ok[u] ? static_cast<int64_t>(blk) * a.bs + cpos % a.bs : 0;
       const T* kp = static_cast<const T*>(a.kc) + layer_base + slot * row_elems + h * D;
       const T* vp = static_cast<const T*>(a.vc) + layer_base + slot * row_elems + h * D;
@@ -489,58 +495,68 @@ __global__ void __launch_bounds__(NW * 32) row_attn_kernel(RowArgs a) {
       }
     }
   };
-  float kv[U][NPL], vv[U][NPL];
-  bool ok[U];
-  load_group(warp * U, kv, vv, ok);
-  for (int c0 = warp * U; c0 < n_ctx; c0 += NW * U) {
-    float kv2[U][NPL], vv2[U][NPL];
-    bool ok2[U];
-    load_group(c0 + NW * U, kv2, vv2, ok2);
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      if (g >= nh) break;
-      float sv[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        float part = 0.f;
-#pragma unroll
-        for (int i = 0; i < NPL; ++i) part = fmaf(q[g][i], kv[u][i], part);
-        sv[u] = part;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int u = 0; u < U; ++u) sv[u] += __shfl_xor_sync(0xffffffffu, sv[u], o);
-      float mx = m[g];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        sv[u] *= a.scale;
-        if (ok[u]) mx = fmaxf(mx, sv[u]);
-      }
-      if (mx == -INFINITY) continue;  // no valid position in the group yet
-      const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mx);
-      l[g] *= alpha;
-#pragma unroll
-      for (int i = 0; i < NPL; ++i) acc[g][i] *= alpha;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (!ok[u]) continue;
-        const float pw = expf(sv[u] - mx);
-        l[g] += pw;
-#pragma unroll
-        for (int i = 0; i < NPL; ++i) acc[g][i] = fmaf(pw, vv[u][i], acc[g][i]);
-      }
-      m[g] = mx;
+  const int pass_pos = kRowPassBlocks * a.bs;
+  for (p0 = 0; p0 < n_ctx; p0 += pass_pos) {
+    pend = min(n_ctx, p0 + pass_pos);
+    {
+      const int b0 = p0 / a.bs, nblk = (pend - p0 + a.bs - 1) / a.bs;
+      for (int b = tid; b < nblk; b += kThreads) blk_s[b] = bt_row[b0 + b];
     }
+    __syncthreads();
+    float kv[U][NPL], vv[U][NPL];
+    bool ok[U];
+    load_group(p0 + warp * U, kv, vv, ok);
+    for (int c0 = p0 + warp * U; c0 < pend; c0 += NW * U) {
+      float kv2[U][NPL], vv2[U][NPL];
+      bool ok2[U];
+      load_group(c0 + NW * U, kv2, vv2, ok2);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      ok[u] = ok2[u];
+      for (int g = 0; g < 8; ++g) {
+        if (g >= nh) break;
+        float sv[U];
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) {
-        kv[u][i] = kv2[u][i];
-        vv[u][i] = vv2[u][i];
+        for (int u = 0; u < U; ++u) {
+          float part = 0.f;
+#pragma unroll
+          for (int i = 0; i < NPL; ++i) part = fmaf(q[g][i], kv[u][i], part);
+          sv[u] = part;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int u = 0; u < U; ++u) sv[u] += __shfl_xor_sync(0xffffffffu, sv[u], o);
+        float mx = m[g];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          sv[u] *= a.scale;
+          if (ok[u]) mx = fmaxf(mx, sv[u]);
+        }
+        if (mx == -INFINITY) continue;  // no valid position in the group yet
+        const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - mx);
+        l[g] *= alpha;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[g][i] *= alpha;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (!ok[u]) continue;
+          const float pw = expf(sv[u] - mx);
+          l[g] += pw;
+#pragma unroll
+          for (int i = 0; i < NPL; ++i) acc[g][i] = fmaf(pw, vv[u][i], acc[g][i]);
+        }
+        m[g] = mx;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        ok[u] = ok2[u];
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+          kv[u][i] = kv2[u][i];
+          vv[u][i] = vv2[u][i];
+        }
       }
     }
+    __syncthreads();  // the next pass rewrites the staged block ids
   }
 
   if (lane == 0) {

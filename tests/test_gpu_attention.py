@@ -145,6 +145,39 @@ def test_decode_small_head_dims_use_cuda_core_path(pkg, oracle, ops):
         _decode_case(pkg, oracle, ops, b, torch.bfloat16, seed=hd)
 
 
+@pytest.mark.parametrize("hd,bs,hq,hkv,ctx", [
+    (64, 16, 12, 12, [1, 4080, 4096, 4097, 5000]),   # 255 / 256 / 257 blocks: one and two passes
+    (128, 1, 8, 2, [1, 255, 256, 257, 700]),         # block size 1: a pass every 256 tokens
+    (32, 5, 16, 4, [3, 1279, 1280, 1281, 2600]),     # odd block size, GQA 4
+    (256, 16, 4, 2, [33, 4100]),                     # head dim 256 (4 warps)
+])
+def test_decode_fp32_row_kernel_passes(pkg, oracle, ops, hd, bs, hq, hkv, ctx):
+    """fp32 caches take the CUDA-core row kernel, which stages a row's block ids 256 at a time:
+    contexts just below, at and above a pass boundary, and several passes, against the oracle
+    within 1e-5 relative."""
+    b = pkg.workloads.custom(seed=hd + bs, context_lens=ctx, new_token_counts=[1] * len(ctx),
+                             num_query_heads=hq, num_kv_heads=hkv, head_dim=hd, block_size=bs)
+    q, kc, vc, bt, cl = device_batch(b, torch.float32, seed=bs)
+    out = ops.paged_decode(q, kc, vc, 0, bt, cl, b.scale, int(b.context_lens.max()))
+    ref = oracle_ragged(oracle, b, q, kc, vc)
+    assert max_rel(out.cpu().numpy(), ref) <= FP32_REL
+    assert ops.read_status(q.device) == 0
+
+
+def test_prefill_fp32_row_kernel_long_context(pkg, oracle, ops):
+    """Ragged fp32 prefill (the row kernel's cu_seqlens form) over prior contexts that cross the
+    block-id staging passes."""
+    b = pkg.workloads.custom(seed=11, context_lens=[4200, 300, 5000], new_token_counts=[40, 300, 7],
+                             num_query_heads=8, num_kv_heads=2, head_dim=64, block_size=16)
+    q, kc, vc, bt, cl = device_batch(b, torch.float32, seed=3)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(b.new_token_counts)]).astype(np.int64))
+    out = ops.paged_prefill(q, kc, vc, 0, bt, cu.to(q.device), cl, b.scale,
+                            int(b.new_token_counts.max()), int(b.context_lens.max()))
+    ref = oracle_ragged(oracle, b, q, kc, vc)
+    assert max_rel(out.cpu().numpy(), ref) <= FP32_REL
+    assert ops.read_status(q.device) == 0
+
+
 def test_decode_strided_query_and_rows(pkg, oracle, ops):
     """HF hands the query over as a transposed view; the kernels take strides, and query_rows
     places each sequence's row (mixed batches)."""
