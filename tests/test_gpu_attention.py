@@ -323,12 +323,12 @@ def test_masked_kernel_random_masks(oracle, ops):
 @pytest.mark.parametrize("d,hq,hkv,density", [(32, 4, 4, 0.5), (64, 8, 2, 0.02), (128, 12, 1, 1.0),
                                               (256, 4, 2, 0.3), (64, 16, 4, 0.7)])
 def test_masked_kernel_multi_pass(oracle, ops, d, hq, hkv, density):
-    """The mask form over contexts longer than one 1024-slot compaction pass (2,500 slots: two
+    """The mask form over contexts longer than one 2048-slot compaction pass (9,000 slots: four
     full passes and a ragged one), every head-dim instantiation (D 32..256), GQA groups of 1 to 12
     (12 = two head chunks per KV head), masks from 2 % to all allowed, a fully masked row, and a
     row whose allowed slots straddle the pass boundaries; fp32, within 1e-5 relative."""
     rng = np.random.default_rng(d + hq + hkv)
-    bs, NB, nq, nctx = 16, 160, 5, 2500
+    bs, NB, nq, nctx = 16, 600, 5, 9000
     kc = rng.standard_normal((1, NB, bs, hkv, d), dtype=np.float32)
     vc = rng.standard_normal((1, NB, bs, hkv, d), dtype=np.float32)
     q = rng.standard_normal((1, hq, nq, d), dtype=np.float32)
@@ -336,8 +336,8 @@ def test_masked_kernel_multi_pass(oracle, ops, d, hq, hkv, density):
     mask = (rng.random((1, 1, nq, nctx)) < density).astype(np.uint8)
     mask[0, 0, 1] = 0
     mask[0, 0, 3] = 0
-    mask[0, 0, 3, 1000:1050] = 1
-    mask[0, 0, 3, 2040:2060] = 1
+    mask[0, 0, 3, 4080:4110] = 1
+    mask[0, 0, 3, 8180:8200] = 1
     ref = oracle.paged_attention(q, kc, vc, 0, gs, mask, 1.0 / np.sqrt(d))
     dev = torch.device("cuda")
     out = ops.paged_attention_masked(torch.from_numpy(q).to(dev), torch.from_numpy(kc).to(dev),
