@@ -460,7 +460,7 @@ def ours_arm(args):
             N.lib().b200_set_prefill_kernel(args.prefill_kernel)
         prefill = prefill_measure(dev, 20, 3,
                                   1 if args.prefill_kernel is None else args.prefill_kernel)
-        prefill["kernel_selector"] = args.prefill_kernel
+        prefill["kernel_selector"] = 1 if args.prefill_kernel is None else args.prefill_kernel
         prefill["long_prompts"] = prefill_long_measure(dev)
     peak, peak_kind = load_peaks()
     ms_per_step = elapsed_ms / args.steps
