@@ -478,13 +478,20 @@ __global__ void __launch_bounds__(NW * 32) row_attn_kernel(RowArgs a) {
   __shared__ int32_t blk_s[kRowPassBlocks];
   int p0 = 0, pend = 0;
   auto load_group = [&](int c0, float (&kv)[U][NPL], float (&vv)[U][NPL], bool (&ok)[U]) {
+    // one division per group: the block index and offset of c0, then stepped position by position
+    int bi = (c0 - p0) / a.bs;
+    int off = (c0 - p0) - bi * a.bs;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int cpos = c0 + u;
-      const int32_t blk = cpos < pend ? blk_s[(cpos - p0) / a.bs] : 0;
+      const int32_t blk = cpos < pend ? blk_s[bi] : 0;
       ok[u] = cpos < pend && blk >= 0 && blk < a.nb;
       if (cpos < pend && !ok[u] && lane == 0) flag_status(a.status, B200_DEVICE_BAD_BLOCK);
-      const int64_t slot = ok[u] ? static_cast<int64_t>(blk) * a.bs + cpos % a.bs : 0;
+      const int64_t slot = ok[u] ? static_cast<int64_t>(blk) * a.bs + off : 0;
+      if (++off == a.bs) {
+        off = 0;
+        ++bi;
+      }
       const T* kp = static_cast<const T*>(a.kc) + layer_base + slot * row_elems + h * D;
       const T* vp = static_cast<const T*>(a.vc) + layer_base + slot * row_elems + h * D;
 #pragma unroll
